@@ -1,0 +1,417 @@
+#!/usr/bin/env python
+"""bench.py -- paged split-KV decode attention on B200: HBM GB/s.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload 256x4096|1x32768|8x8192|64x1024|ragged256]
+
+One step = one ckl_decode_attention call (the C-ABI entry point; partial kernel + LSE
+merge when the batch is split) over one synthetic paged batch: Hq=32, Hkv=8, d=128, page
+16, shuffled page table, K/V U(-1,1) fp16 filled on the device. The default workload is
+B=256 x L=4096 (4.3 GB of KV, larger than the 126 MB L2, so no flush is needed between
+steps). Under torchrun (N>1) every rank decodes its own batch of the same shape (weak
+scaling by sequence; no collective on the data path); timing is CUDA events, max over ranks.
+
+Rank 0 prints one JSON line. `value` = algorithmic bytes of all ranks / max step time
+(sum of K+V of every token + q + out + lse); `e2e` = the same metric with the per-step
+host->device copy of q and the page table from pinned memory and the device->host read of
+out and lse inside the timed region; `roofline` = the partial kernel's achieved GB/s
+against the measured HBM copy bandwidth (MEASURED_PEAKS.json); `cpu_baseline` = the
+reference's own fp64 cpu_reference (oracle/_ref) on the host cores, on a bounded sample.
+
+--impl reference times the reference's CPU implementation of the path (the same
+cpu_reference) on the same workload shape, one bounded sample per step, all host threads.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "cuda-kernel-lab_b200"))
+
+HQ, HKV, D, PAGE = 32, 8, 128, 16
+WORKLOADS = {
+    "256x4096": dict(B=256, L=4096),
+    "1x32768": dict(B=1, L=32768),
+    "8x8192": dict(B=8, L=8192),
+    "64x1024": dict(B=64, L=1024),
+    "ragged256": dict(B=256, L=None),   # lengths U[128, 8192], seeded
+}
+METRIC = "decode-attn HBM GB/s"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="256x4096")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def lengths(workload, seed=2024):
+    import numpy as np
+    w = WORKLOADS[workload]
+    if w["L"] is None:
+        return np.random.default_rng(seed).integers(128, 8193, size=w["B"]).astype(np.int32)
+    return np.full(w["B"], w["L"], np.int32)
+
+
+def algorithmic_bytes(lens):
+    kv = int(sum(int(L) for L in lens)) * HKV * D * 2 * 2
+    return kv + len(lens) * HQ * D * 2 * 2 + len(lens) * HQ * 4
+
+
+def config_of(workload, lens, n):
+    return {"workload": f"paged GQA decode attention {workload}", "B": int(len(lens)),
+            "L": "U[128,8192]" if WORKLOADS[workload]["L"] is None else int(lens[0]),
+            "Hq": HQ, "Hkv": HKV, "head_dim": D, "page": PAGE, "page_table": "shuffled",
+            "kv_dtype": "fp16", "per_rank": "own batch (weak scaling by sequence)",
+            "l2": "inputs larger than L2 (KV %.2f GB > 126 MB), no flush" %
+                  (algorithmic_bytes(lens) / 1e9), "parallelism": f"replicas x{n}"}
+
+
+# ------------------------------------------------------------------ clocks
+class Clocks:
+    """nvidia-smi samples during the timed region."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.idx = gpu_index
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                       "-lms", "200", "-i", str(gpu_index)], stdout=self.f,
+                                      stderr=subprocess.DEVNULL)
+        except OSError:
+            self.p = None
+
+    def stop(self):
+        if self.p is None:
+            return None
+        self.p.terminate()
+        try:
+            self.p.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.p.kill()
+        self.f.seek(0)
+        rows = [r.split(", ") for r in self.f.read().strip().splitlines() if r.strip()]
+        os.unlink(self.f.name)
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            try:
+                sm.append(float(r[1]))
+                mx = max(mx, float(r[2]))
+                for n, v in zip(names, r[5:9]):
+                    if v.strip() == "Active":
+                        reasons.add(n)
+            except (ValueError, IndexError):
+                continue
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ------------------------------------------------------------------ distributed plumbing
+def dist_setup(n):
+    import torch
+    import torch.distributed as dist
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != n:
+        sys.exit(f"--gpus {n} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=180),
+                                device_id=torch.device("cuda", local))
+    return rank, world, local
+
+
+def barrier(world):
+    import torch
+    import torch.distributed as dist
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+def max_over_ranks(x, world):
+    import torch
+    import torch.distributed as dist
+    if world == 1:
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def measured_peak():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            pk = json.load(f)
+        return float(pk["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, "fallback"
+
+
+def committed_traffic(kernel, workload):
+    """DRAM bytes per launch from a committed ncu summary (profiles/traffic.json)."""
+    try:
+        with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
+            t = json.load(f)
+        e = t.get(kernel, {}).get(workload)
+        return None if e is None else float(e)
+    except (OSError, ValueError):
+        return None
+
+
+# ------------------------------------------------------------------ CPU baselines
+def cpu_baseline_sample(L, threads, min_seqs=64):
+    """The reference's cpu_reference (oracle/_ref) on `threads` threads over a bounded
+    sample of ~min_seqs sequences of length L; returns the cpu_baseline object."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    if O.ref01() is not None:
+        bpt = max(1, math.ceil(min_seqs / threads))
+        s = O.RefCpuSample(threads, bpt, L, HQ, HKV, seed=11)
+        try:
+            sec, kvb = s.run()
+        finally:
+            s.close()
+        nseq = threads * bpt
+        byts = kvb + nseq * HQ * D * 2 * 2 + nseq * HQ * 4
+        return {"value": byts / sec / 1e9, "unit": "GB/s", "cores": threads, "kind": "reference",
+                "sample": f"{nseq} sequences x L={L} (Hq={HQ}, Hkv={HKV}), {threads} threads x "
+                          f"{bpt}; cpu_reference 01_decode_attention.cu:371-400 compiled from "
+                          f"the reference sources; {sec:.2f} s"}
+    bt = O.batch([L] * 8, HQ, HKV, 11)
+    sec = O.port_attention_seconds(bt, threads)
+    return {"value": algorithmic_bytes([L] * 8) / sec / 1e9, "unit": "GB/s", "cores": threads,
+            "kind": "port", "sample": f"8 sequences x L={L}, oracle port, {sec:.2f} s"}
+
+
+def run_reference(args):
+    rank, world, local = int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")), 0
+    if rank != 0:
+        return 0
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    lens = lengths(args.workload)
+    L = int(lens.max()) if WORKLOADS[args.workload]["L"] is None else int(lens[0])
+    threads = os.cpu_count() or 1
+    if O.ref01() is None:
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref not built (the reference "
+                          "sources were not present when this tree was built)"}))
+        return 0
+    s = O.RefCpuSample(threads, 1, L, HQ, HKV, seed=11)
+    try:
+        for _ in range(args.warmup):
+            s.run()
+        secs = []
+        kvb = 0.0
+        for _ in range(args.steps):
+            sec, kvb = s.run()
+            secs.append(sec)
+    finally:
+        s.close()
+    nseq = threads
+    byts = kvb + nseq * HQ * D * 2 * 2 + nseq * HQ * 4
+    tot = sum(secs)
+    val = byts * len(secs) / tot / 1e9
+    line = {"metric": METRIC, "value": val, "unit": "GB/s", "impl": "reference",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": tot / len(secs) * 1e3, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f64", "data": "synthetic (reference generator)",
+            "config": config_of(args.workload, lens, args.gpus),
+            "cpu_baseline": {"value": val, "unit": "GB/s", "cores": threads, "kind": "reference",
+                             "sample": f"per step {nseq} sequences x L={L} (one per thread) of "
+                                       "the workload; cpu_reference compiled from the reference"},
+            "e2e": {"value": val, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line))
+    return 0
+
+
+# ------------------------------------------------------------------ our arm
+def run_ours(args):
+    import numpy as np
+    import torch
+    import ckl
+
+    rank, world, local = dist_setup(args.gpus)
+    dev = torch.device("cuda", local)
+    lens = lengths(args.workload)
+    B = len(lens)
+    npg = (lens + PAGE - 1) // PAGE
+    indptr = np.zeros(B + 1, np.int32)
+    indptr[1:] = np.cumsum(npg)
+    last = (lens - (npg - 1) * PAGE).astype(np.int32)
+    num_pages = int(indptr[-1])
+    rng = np.random.default_rng(1000 + rank)
+    indices = rng.permutation(num_pages).astype(np.int32)
+
+    g = torch.Generator(device=dev)
+    g.manual_seed(1000 + rank)
+    k = torch.empty((num_pages, PAGE, HKV, D), dtype=torch.float16, device=dev)
+    v = torch.empty_like(k)
+    for t in (k, v):   # chunked U(-1,1) fill keeps the fp32 temporary small
+        flat = t.view(-1)
+        step = 1 << 28
+        for s0 in range(0, flat.numel(), step):
+            n = min(step, flat.numel() - s0)
+            flat[s0:s0 + n] = (torch.rand(n, generator=g, device=dev) * 2 - 1).half()
+    q_host = (torch.rand((B, HQ, D), generator=g, device=dev) * 2 - 1).half().cpu().pin_memory()
+    d_q = q_host.to(dev)
+    d_indptr = torch.from_numpy(indptr).to(dev)
+    d_indices = torch.from_numpy(indices).to(dev)
+    d_last = torch.from_numpy(last).to(dev)
+    nc, ct = ckl.plan_chunks(HQ // HKV, B, HKV, int(lens.max()))
+    p = ckl.make_params(d_q, k, v, d_indptr, d_indices, d_last, num_chunks=nc, chunk_tokens=ct)
+    out = torch.empty_like(d_q)
+    lse = torch.empty((B, HQ), dtype=torch.float32, device=dev)
+    ws_n = ckl.workspace_size(p)
+    ws = torch.empty(max(ws_n, 256), dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream()
+    launches_per_step = 1 if nc == 1 else 2
+    byts = algorithmic_bytes(lens)
+
+    import ctypes as C
+    L = ckl.lib()
+    sptr = C.c_void_p(stream.cuda_stream)
+
+    def step():
+        ckl.check(L.ckl_decode_attention(C.byref(p), C.c_void_p(out.data_ptr()),
+                                         C.c_void_p(lse.data_ptr()), C.c_void_p(ws.data_ptr()),
+                                         ws.numel(), sptr), "ckl_decode_attention")
+
+    # ---- device-resident timing (value)
+    for _ in range(args.warmup):
+        step()
+    barrier(world)
+    clocks = Clocks(local)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    barrier(world)
+    ms = e0.elapsed_time(e1) / args.steps
+    clk = clocks.stop()
+    ms_max = max_over_ranks(ms, world)
+    ckl.check_device_error()
+
+    # ---- dominant kernel alone (the partial kernel), for the roofline
+    if nc == 1:
+        kern_ms = ms
+    else:
+        pp = ckl.make_params(d_q, k, v, d_indptr, d_indices, d_last, num_chunks=nc,
+                             chunk_tokens=ct)
+        po_bytes = ((B * HQ * nc * D * 4 + 255) // 256) * 256   # workspace layout
+        pp.part_o = ws.data_ptr()
+        pp.part_lse = ws.data_ptr() + po_bytes
+        for _ in range(3):
+            ckl.decode_partial(pp)
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for _ in range(args.steps):
+            ckl.decode_partial(pp)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        kern_ms = e0.elapsed_time(e1) / args.steps
+
+    # ---- end to end through the C-ABI with host buffers
+    h_indptr = torch.from_numpy(indptr).pin_memory()
+    h_indices = torch.from_numpy(indices).pin_memory()
+    h_last = torch.from_numpy(last).pin_memory()
+    h_out = torch.empty((B, HQ, D), dtype=torch.float16).pin_memory()
+    h_lse = torch.empty((B, HQ), dtype=torch.float32).pin_memory()
+    h2d = q_host.numel() * 2 + h_indptr.numel() * 4 + h_indices.numel() * 4 + h_last.numel() * 4
+    d2h = h_out.numel() * 2 + h_lse.numel() * 4
+
+    def e2e_step():
+        d_q.copy_(q_host, non_blocking=True)
+        d_indptr.copy_(h_indptr, non_blocking=True)
+        d_indices.copy_(h_indices, non_blocking=True)
+        d_last.copy_(h_last, non_blocking=True)
+        step()
+        h_out.copy_(out, non_blocking=True)
+        h_lse.copy_(lse, non_blocking=True)
+
+    for _ in range(args.warmup):
+        e2e_step()
+    barrier(world)
+    e0.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record(stream)
+    barrier(world)
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, world)
+
+    # correctness of what was timed: a sampled sequence against a plain fp32 torch check
+    b0 = 0
+    pages = indices[indptr[b0]:indptr[b0 + 1]]
+    kk = k[torch.from_numpy(pages.astype(np.int64)).to(dev)].reshape(-1, HKV, D)[:lens[b0]].float()
+    vv = v[torch.from_numpy(pages.astype(np.int64)).to(dev)].reshape(-1, HKV, D)[:lens[b0]].float()
+    qq = d_q[b0].float().view(HKV, HQ // HKV, D)
+    s_ = torch.einsum("hgd,lhd->hgl", qq, kk) / math.sqrt(D)
+    ref = torch.einsum("hgl,lhd->hgd", torch.softmax(s_, -1), vv).reshape(HQ, D)
+    chk_err = float((out[b0].float() - ref).abs().max())
+
+    peak, peak_kind = measured_peak()
+    achieved = byts / (kern_ms * 1e-3) / 1e9
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline_sample(int(lens.max()), os.cpu_count() or 1)
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": byts * world / (ms_max * 1e-3) / 1e9, "unit": "GB/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_max,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp16",
+            "data": "synthetic: U(-1,1) fp16 K/V/q filled on device, seeded shuffled page table",
+            "config": config_of(args.workload, lens, world),
+            "frac_of_hbm": byts * world / (ms_max * 1e-3) / 1e9 / (peak * world),
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "peak_source": peak_kind,
+                         "kernel": "decode_partial_kernel<4>",
+                         "algorithmic_bytes_per_launch": byts,
+                         "traffic": committed_traffic("decode_partial_kernel<4>", args.workload)},
+            "e2e": {"value": byts * world / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s",
+                    "ms_per_step": e2e_ms, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "gpu_launches": launches_per_step * args.steps,
+            "plan": {"num_chunks": nc, "chunk_tokens": ct},
+            "check_max_abs_err_vs_fp32": chk_err,
+            "cpu_baseline": cpu,
+            "clocks": clk,
+        }
+        print(json.dumps(line))
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

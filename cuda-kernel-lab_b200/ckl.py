@@ -1,0 +1,223 @@
+"""Python host mirror of the reference's decode-layer interface, over the C ABI.
+
+Every call goes through libckl.so (include/ckl.h); there is no CPU or PyTorch fallback:
+if the library is missing or a call fails, a CklError is raised. PyTorch is used only as
+plumbing -- device tensors, streams -- and tensors cross the boundary as raw pointers.
+
+Names follow the reference (01_decode_attention.cu, 03_moe_wq_decode.cu, common/moe.cuh):
+plan_chunks, decode_attention, merge_states, shared_prefix_pages, plan_cascade,
+cascade_decode, ...
+"""
+from __future__ import annotations
+
+import ctypes as C
+import math
+import os
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libckl.so")
+HEAD_DIM = 128
+PAGE = 16
+
+CKL_OK = 0
+STATUS = {0: "CKL_OK", 1: "CKL_INVALID_ARG", 2: "CKL_UNSUPPORTED_SHAPE", 3: "CKL_CUDA_ERROR",
+          4: "CKL_NCCL_ERROR", 5: "CKL_TIMEOUT", 6: "CKL_WORKSPACE_TOO_SMALL"}
+
+
+class CklError(RuntimeError):
+    def __init__(self, status, where, msg):
+        self.status = status
+        super().__init__(f"{where}: {STATUS.get(status, status)}: {msg}")
+
+
+class DecodeParams(C.Structure):
+    """ckl_decode_params (mirrors DecodeParams, 01_decode_attention.cu:51-65)."""
+    _fields_ = [("q", C.c_void_p), ("k_cache", C.c_void_p), ("v_cache", C.c_void_p),
+                ("kv_indptr", C.c_void_p), ("kv_indices", C.c_void_p),
+                ("kv_last_page_len", C.c_void_p), ("part_o", C.c_void_p),
+                ("part_lse", C.c_void_p), ("B", C.c_int), ("Hq", C.c_int), ("Hkv", C.c_int),
+                ("num_chunks", C.c_int), ("chunk_tokens", C.c_int), ("kv_start", C.c_int),
+                ("chunk_base", C.c_int), ("part_stride", C.c_int), ("sm_scale", C.c_float),
+                ("num_pages", C.c_int)]
+
+
+_lib = None
+
+# name -> (restype, argtypes); every function declared in include/ckl.h
+_SIGS = {
+    "ckl_last_error_string": (C.c_char_p, []),
+    "ckl_version": (C.c_char_p, []),
+    "ckl_check_device_error": (C.c_int, []),
+    "ckl_set_spin_timeout_ns": (None, [C.c_uint64]),
+    "ckl_decode_plan": (C.c_int, [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
+                                  C.POINTER(C.c_int), C.POINTER(C.c_int)]),
+    "ckl_decode_workspace_size": (C.c_size_t, [C.POINTER(DecodeParams)]),
+    "ckl_decode_partial": (C.c_int, [C.POINTER(DecodeParams), C.c_void_p]),
+    "ckl_merge_states": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int,
+                                   C.c_int, C.c_void_p]),
+    "ckl_decode_attention": (C.c_int, [C.POINTER(DecodeParams), C.c_void_p, C.c_void_p,
+                                       C.c_void_p, C.c_size_t, C.c_void_p]),
+    "ckl_validate_page_table": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int,
+                                          C.c_int]),
+    "ckl_stream_read": (C.c_int, [C.c_void_p, C.c_size_t, C.c_void_p, C.c_void_p]),
+}
+
+
+def lib():
+    """Loads libckl.so (raises if it was not built: there is no fallback)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise CklError(3, "load", f"{LIB_PATH} not built (run make -C cuda-kernel-lab_b200)")
+        L = C.CDLL(LIB_PATH)
+        for name, (res, args) in _SIGS.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def check(status, where):
+    if status != CKL_OK:
+        msg = lib().ckl_last_error_string().decode(errors="replace")
+        raise CklError(status, where, msg)
+
+
+def version():
+    return lib().ckl_version().decode()
+
+
+def check_device_error():
+    check(lib().ckl_check_device_error(), "ckl_check_device_error")
+
+
+def set_spin_timeout_ns(ns):
+    lib().ckl_set_spin_timeout_ns(int(ns))
+
+
+# ------------------------------------------------------------------ torch plumbing
+def _torch():
+    import torch
+    return torch
+
+
+def _ptr(t):
+    return None if t is None else C.c_void_p(t.data_ptr())
+
+
+def _stream(stream):
+    torch = _torch()
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return C.c_void_p(s.cuda_stream)
+
+
+def _need(t, dtype, name):
+    torch = _torch()
+    if t is None or not isinstance(t, torch.Tensor) or not t.is_cuda:
+        raise CklError(1, name, "expected a CUDA tensor")
+    if t.dtype != dtype or not t.is_contiguous():
+        raise CklError(1, name, f"expected contiguous {dtype}, got {t.dtype}")
+    return t
+
+
+# ------------------------------------------------------------------ decode attention
+def plan_chunks(G, B, Hkv, max_len, force_chunks=0):
+    """plan_chunks (01_decode_attention.cu:292-312) -> (num_chunks, chunk_tokens)."""
+    nc, ct = C.c_int(), C.c_int()
+    check(lib().ckl_decode_plan(G, B, Hkv, max_len, force_chunks, C.byref(nc), C.byref(ct)),
+          "ckl_decode_plan")
+    return nc.value, ct.value
+
+
+def make_params(q, k_cache, v_cache, kv_indptr, kv_indices, kv_last_page_len, *, num_chunks,
+                chunk_tokens, kv_start=0, chunk_base=0, part_stride=None, sm_scale=None,
+                part_o=None, part_lse=None):
+    torch = _torch()
+    _need(q, torch.float16, "q")
+    _need(k_cache, torch.float16, "k_cache")
+    _need(v_cache, torch.float16, "v_cache")
+    for t, n in ((kv_indptr, "kv_indptr"), (kv_indices, "kv_indices"),
+                 (kv_last_page_len, "kv_last_page_len")):
+        _need(t, torch.int32, n)
+    B, Hq, D = q.shape
+    num_pages, page, Hkv, D2 = k_cache.shape
+    if D != HEAD_DIM or D2 != HEAD_DIM or page != PAGE or v_cache.shape != k_cache.shape:
+        raise CklError(2, "make_params", f"q {tuple(q.shape)} / cache {tuple(k_cache.shape)}")
+    p = DecodeParams()
+    p.q, p.k_cache, p.v_cache = q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr()
+    p.kv_indptr, p.kv_indices = kv_indptr.data_ptr(), kv_indices.data_ptr()
+    p.kv_last_page_len = kv_last_page_len.data_ptr()
+    p.part_o = None if part_o is None else part_o.data_ptr()
+    p.part_lse = None if part_lse is None else part_lse.data_ptr()
+    p.B, p.Hq, p.Hkv = B, Hq, Hkv
+    p.num_chunks, p.chunk_tokens = num_chunks, chunk_tokens
+    p.kv_start, p.chunk_base = kv_start, chunk_base
+    p.part_stride = num_chunks + chunk_base if part_stride is None else part_stride
+    p.sm_scale = 1.0 / math.sqrt(HEAD_DIM) if sm_scale is None else sm_scale
+    p.num_pages = num_pages
+    return p
+
+
+def workspace_size(p: DecodeParams):
+    return lib().ckl_decode_workspace_size(C.byref(p))
+
+
+def decode_partial(p: DecodeParams, stream=None):
+    check(lib().ckl_decode_partial(C.byref(p), _stream(stream)), "ckl_decode_partial")
+
+
+def merge_states(part_o, part_lse, out, lse, stream=None):
+    rows, slots = part_lse.shape[0], part_lse.shape[1]
+    check(lib().ckl_merge_states(_ptr(part_o), _ptr(part_lse), _ptr(out), _ptr(lse), rows,
+                                 slots, _stream(stream)), "ckl_merge_states")
+
+
+def decode_attention(q, k_cache, v_cache, kv_indptr, kv_indices, kv_last_page_len, *,
+                     max_len=None, force_chunks=0, num_chunks=None, chunk_tokens=None,
+                     out=None, lse=None, workspace=None, sm_scale=None, stream=None):
+    """decode_attention (01_decode_attention.cu:316-331): returns (out fp16 [B,Hq,128],
+    lse fp32 [B,Hq]). Plans the split like the reference (plan_chunks) unless num_chunks /
+    chunk_tokens are given; max_len defaults to the longest sequence (read from the page
+    table on the host, which synchronises)."""
+    torch = _torch()
+    B, Hq, _ = q.shape
+    Hkv = k_cache.shape[2]
+    if num_chunks is None:
+        if max_len is None:
+            ip = kv_indptr.cpu()
+            lp = kv_last_page_len.cpu()
+            np_ = ip[1:] - ip[:-1]
+            lens = torch.where(np_ > 0, (np_ - 1) * PAGE + lp, torch.zeros_like(np_))
+            max_len = int(lens.max()) if B else 0
+        num_chunks, chunk_tokens = plan_chunks(Hq // Hkv, B, Hkv, max_len, force_chunks)
+    p = make_params(q, k_cache, v_cache, kv_indptr, kv_indices, kv_last_page_len,
+                    num_chunks=num_chunks, chunk_tokens=chunk_tokens, sm_scale=sm_scale)
+    if out is None:
+        out = torch.empty_like(q)
+    if lse is None:
+        lse = torch.empty((B, Hq), dtype=torch.float32, device=q.device)
+    need = workspace_size(p)
+    if need and (workspace is None or workspace.numel() * workspace.element_size() < need):
+        workspace = torch.empty(need, dtype=torch.uint8, device=q.device)
+    ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
+    check(lib().ckl_decode_attention(C.byref(p), _ptr(out), _ptr(lse), _ptr(workspace),
+                                     ws_bytes, _stream(stream)), "ckl_decode_attention")
+    return out, lse
+
+
+def validate_page_table(indptr, indices, last, num_pages):
+    """Host validation of a page table given as numpy int32 arrays."""
+    import numpy as np
+    ip = np.ascontiguousarray(indptr, dtype=np.int32)
+    ix = np.ascontiguousarray(indices, dtype=np.int32)
+    ls = np.ascontiguousarray(last, dtype=np.int32)
+    check(lib().ckl_validate_page_table(ip.ctypes.data_as(C.c_void_p),
+                                        ix.ctypes.data_as(C.c_void_p),
+                                        ls.ctypes.data_as(C.c_void_p), len(ip) - 1, num_pages),
+          "ckl_validate_page_table")
+
+
+def stream_read(buf, sink, stream=None):
+    check(lib().ckl_stream_read(_ptr(buf), buf.numel() * buf.element_size(), _ptr(sink),
+                                _stream(stream)), "ckl_stream_read")

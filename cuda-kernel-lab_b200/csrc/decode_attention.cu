@@ -1,0 +1,595 @@
+// decode_attention.cu -- paged split-KV GQA decode attention for sm_100a.
+//
+// Replaces decode_partial<G,V> / merge_states / plan_chunks / decode_attention of the
+// reference (01_decode_attention.cu:77-331) with a B200-native design:
+//
+//   * One CTA per (sequence b, kv head, chunk). Warp 4 is a producer: it reads the chunk's
+//     page ids and issues TMA tiled loads (cp.async.bulk.tensor.4d, 128B swizzle, evict-
+//     first L2 hint) of whole pages -- 16 keys x 128 dims of K and of V for this head, 4 KB
+//     each -- into an 8-stage shared-memory ring guarded by full/empty mbarriers. 64 KB are
+//     in flight per CTA, two CTAs per SM.
+//   * Warps 0..3 consume pages round-robin. Per page a warp computes S = Q K^T for its G
+//     query heads (the GQA group, padded to the 16 rows of an m16n8k16 tile) with
+//     mma.sync (K fragments by ldmatrix from the swizzled tile, q fragments held in
+//     registers), an online softmax in the log2 domain with a lazy rescale, and O += P V
+//     (V fragments by ldmatrix.trans). Tensor-core math leaves the kernel bound by HBM:
+//     per 16-key page a warp issues 32 MMAs and 16 ldmatrix, against ~700 warp
+//     instructions for the reference's CUDA-core dot products.
+//   * The four warps' (m, l, O) states are merged through shared memory; a single-chunk
+//     launch writes the final fp16 out and lse directly, otherwise normalised fp32 partials
+//     (o, lse) go to the caller's workspace for the LSE merge kernel.
+//
+// Page-table convention (01_decode_attention.cu:5-9, 93-95, 111-112): seq_len =
+// (npages-1)*16 + last_page_len, key -> page kv_indices[indptr[b] + key/16], element
+// ((page*16 + key%16)*Hkv + kvh)*128 + d.
+
+#include <cmath>
+#include <cstring>
+#include <mutex>
+
+#include "ckl_internal.h"
+#include "ckl_ptx.cuh"
+
+namespace ckl {
+namespace attn {
+
+constexpr int D = CKL_HEAD_DIM;
+constexpr int PAGE = CKL_PAGE_SIZE;
+constexpr int CONSUMERS = 4;
+constexpr int THREADS = (CONSUMERS + 1) * 32;
+constexpr int STAGES = 8;
+constexpr int HALF_TILE = PAGE * 64 * 2;  // 16 keys x 64 dims fp16 = 2 KB, 128B-swizzled
+constexpr int KV_TILE = 2 * HALF_TILE;    // one page of K (or V) for one head: 4 KB
+constexpr int STAGE_BYTES = 2 * KV_TILE;  // K + V
+constexpr int RING_BYTES = STAGES * STAGE_BYTES;
+constexpr int BAR_BYTES = 2 * STAGES * 8;
+constexpr int RED_BYTES = 2 * CONSUMERS * 16 * 4;
+constexpr int SMEM_BYTES = 1024 /*alignment slack*/ + RING_BYTES + BAR_BYTES + RED_BYTES;
+constexpr float LOG2E = 1.4426950408889634f;
+constexpr float LN2 = 0.6931471805599453f;
+constexpr float RESCALE_THRESHOLD = 8.f;   // log2 units: p may grow to 2^8 before a rescale
+
+struct Args {
+    const __half* q;
+    const int* indptr;
+    const int* indices;
+    const int* last;
+    float* part_o;
+    float* part_lse;
+    __half* out;
+    float* lse;
+    unsigned* err;
+    unsigned long long timeout_ns;
+    int B, Hq, Hkv, chunk_tokens, kv_start, chunk_base, part_stride, direct;
+    float scale_log2;
+};
+
+// Byte offset of 16-byte chunk `cd` (0..15, dims 8cd..8cd+7) of key `key` inside a page
+// tile: [half = cd/8][key][64 dims] with the TMA 128B swizzle (chunk ^= key%8 within each
+// 128-byte row; the tile is 1024-byte aligned).
+__device__ __forceinline__ uint32_t tile_off(int key, int cd) {
+    const int c = cd & 7;
+    return (uint32_t)((cd >> 3) * HALF_TILE + key * 128 + ((c ^ (key & 7)) << 4));
+}
+
+template <int G>
+__global__ void __launch_bounds__(THREADS, 2)
+decode_partial_kernel(const __grid_constant__ CUtensorMap tmK,
+                      const __grid_constant__ CUtensorMap tmV, const Args a) {
+    static_assert(G == 1 || G == 2 || G == 4 || G == 8 || G == 16, "GQA group size");
+    constexpr bool HI = G > 8;   // rows 8..15 of the MMA tile carry query heads too
+
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* ring = align_ptr<1024>(smem_raw);
+    uint64_t* full = reinterpret_cast<uint64_t*>(ring + RING_BYTES);
+    uint64_t* empty = full + STAGES;
+    float* m_red = reinterpret_cast<float*>(empty + STAGES);   // [CONSUMERS][16]
+    float* l_red = m_red + CONSUMERS * 16;                      // [CONSUMERS][16]
+
+    const int bh = blockIdx.x, chunk = blockIdx.y;
+    const int b = bh / a.Hkv, kvh = bh - b * a.Hkv;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+    const int page_beg = __ldg(a.indptr + b);
+    const int npages = __ldg(a.indptr + b + 1) - page_beg;
+    const int seq_len = npages > 0 ? (npages - 1) * PAGE + __ldg(a.last + b) : 0;
+    const int kbeg = a.kv_start + chunk * a.chunk_tokens;       // multiple of 16
+    const int kend = min(seq_len, kbeg + a.chunk_tokens);
+    const int p0 = kbeg / PAGE;
+    const int npg = kend > kbeg ? (kend - kbeg + PAGE - 1) / PAGE : 0;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        fence_barrier_init();
+    }
+    __syncthreads();
+    const uint64_t deadline = globaltimer() + a.timeout_ns;
+
+    // consumer state (unused by the producer warp)
+    float o[16][4];
+    float m_lo = -INFINITY, m_hi = -INFINITY, l_lo = 0.f, l_hi = 0.f;
+    const int g = lane >> 2, t = lane & 3;
+
+    if (warp == CONSUMERS) {
+        // ---------------------------------------------------------------- producer warp
+        if (lane == 0) {
+            tma_prefetch_desc(&tmK);
+            tma_prefetch_desc(&tmV);
+        }
+        const uint64_t pol = policy_evict_first();
+        int ok = 1, issued = 0;
+        for (int base = 0; base < npg && ok; base += 32) {
+            const int cnt = min(32, npg - base);
+            const int my_page = lane < cnt ? __ldg(a.indices + page_beg + p0 + base + lane) : 0;
+            for (int j = 0; j < cnt; j++) {
+                const int page = __shfl_sync(0xffffffffu, my_page, j);
+                if (lane == 0) {
+                    const int i = base + j, s = i % STAGES;
+                    if (i >= STAGES) ok = mbar_wait(&empty[s], ((i / STAGES) - 1) & 1, deadline, a.err);
+                    if (ok) {
+                        uint8_t* st = ring + s * STAGE_BYTES;
+                        mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
+                        tma_load_4d(st, &tmK, 0, kvh, 0, page, &full[s], pol);
+                        tma_load_4d(st + HALF_TILE, &tmK, 64, kvh, 0, page, &full[s], pol);
+                        tma_load_4d(st + KV_TILE, &tmV, 0, kvh, 0, page, &full[s], pol);
+                        tma_load_4d(st + KV_TILE + HALF_TILE, &tmV, 64, kvh, 0, page, &full[s], pol);
+                        issued = i + 1;
+                    }
+                }
+                ok = __shfl_sync(0xffffffffu, ok, 0);
+                if (!ok) break;
+            }
+        }
+        // Every issued copy must land before the CTA reuses the ring or exits.
+        if (lane == 0) {
+            for (int s = 0; s < STAGES && s < issued; s++) {
+                const int i_last = s + ((issued - 1 - s) / STAGES) * STAGES;
+                mbar_wait(&full[s], (i_last / STAGES) & 1, deadline, a.err);
+            }
+        }
+    } else {
+        // ---------------------------------------------------------------- consumer warps
+        // q fragments (A operand: rows = the G query heads of this kv head, cols = dims)
+        uint32_t qa0[8], qa1[8], qa2[8], qa3[8];
+#pragma unroll
+        for (int kk = 0; kk < 8; kk++) qa0[kk] = qa1[kk] = qa2[kk] = qa3[kk] = 0u;
+        if (g < G) {
+            const uint32_t* qrow = reinterpret_cast<const uint32_t*>(
+                a.q + ((size_t)b * a.Hq + (size_t)kvh * G + g) * D);
+#pragma unroll
+            for (int kk = 0; kk < 8; kk++) {
+                qa0[kk] = __ldg(qrow + 8 * kk + t);
+                qa2[kk] = __ldg(qrow + 8 * kk + 4 + t);
+            }
+            if (HI) {
+                const uint32_t* qhi = qrow + 8 * D / 2;
+#pragma unroll
+                for (int kk = 0; kk < 8; kk++) {
+                    qa1[kk] = __ldg(qhi + 8 * kk + t);
+                    qa3[kk] = __ldg(qhi + 8 * kk + 4 + t);
+                }
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < 16; j++) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+
+        // ldmatrix lane addressing (see tile_off): K as the B operand of Q K^T, non-trans:
+        // lanes 0-7 keys 0-7 / dims 16kk..+7, 8-15 keys 0-7 / +8..15, 16-31 keys 8-15.
+        const int k_key = (lane & 7) + ((lane >> 4) << 3), k_hi = (lane >> 3) & 1;
+        // V as the B operand of P V, transposed: lanes 0-7 keys 0-7, 8-15 keys 8-15 of dim
+        // chunk 2jj, lanes 16-31 the same for chunk 2jj+1.
+        const int v_key = (lane & 7) + (((lane >> 3) & 1) << 3), v_hi = lane >> 4;
+
+        bool ok = true;
+        for (int i = warp; i < npg; i += CONSUMERS) {
+            const int s = i % STAGES;
+            const bool got = mbar_wait(&full[s], (i / STAGES) & 1, deadline, a.err);
+            if (!__all_sync(0xffffffffu, got)) { ok = false; break; }
+            const uint32_t kb = smem_u32(ring + s * STAGE_BYTES);
+            const uint32_t vb = kb + KV_TILE;
+
+            float sc[2][4];
+#pragma unroll
+            for (int n = 0; n < 2; n++) sc[n][0] = sc[n][1] = sc[n][2] = sc[n][3] = 0.f;
+#pragma unroll
+            for (int kk = 0; kk < 8; kk++) {
+                uint32_t b00, b01, b10, b11;
+                ldmatrix_x4(kb + tile_off(k_key, 2 * kk + k_hi), b00, b01, b10, b11);
+                mma_16816(sc[0], qa0[kk], qa1[kk], qa2[kk], qa3[kk], b00, b01);
+                mma_16816(sc[1], qa0[kk], qa1[kk], qa2[kk], qa3[kk], b10, b11);
+            }
+            // mask keys past the chunk end (only the sequence's last page is partial)
+            const int kbase = (p0 + i) * PAGE;
+            if (kbase + PAGE > kend) {
+#pragma unroll
+                for (int n = 0; n < 2; n++)
+#pragma unroll
+                    for (int c = 0; c < 4; c++)
+                        if (kbase + n * 8 + 2 * t + (c & 1) >= kend) sc[n][c] = -INFINITY;
+            }
+#pragma unroll
+            for (int n = 0; n < 2; n++)
+#pragma unroll
+                for (int c = 0; c < 4; c++) sc[n][c] *= a.scale_log2;
+
+            float mx_lo = fmaxf(fmaxf(sc[0][0], sc[0][1]), fmaxf(sc[1][0], sc[1][1]));
+            mx_lo = fmaxf(mx_lo, __shfl_xor_sync(0xffffffffu, mx_lo, 1));
+            mx_lo = fmaxf(mx_lo, __shfl_xor_sync(0xffffffffu, mx_lo, 2));
+            float mx_hi = -INFINITY;
+            if (HI) {
+                mx_hi = fmaxf(fmaxf(sc[0][2], sc[0][3]), fmaxf(sc[1][2], sc[1][3]));
+                mx_hi = fmaxf(mx_hi, __shfl_xor_sync(0xffffffffu, mx_hi, 1));
+                mx_hi = fmaxf(mx_hi, __shfl_xor_sync(0xffffffffu, mx_hi, 2));
+            }
+            const bool need = mx_lo > m_lo + RESCALE_THRESHOLD || (HI && mx_hi > m_hi + RESCALE_THRESHOLD);
+            if (__any_sync(0xffffffffu, need)) {
+                const float mn_lo = fmaxf(m_lo, mx_lo);
+                const float c_lo = ex2(m_lo - mn_lo);
+                m_lo = mn_lo;
+                l_lo *= c_lo;
+#pragma unroll
+                for (int j = 0; j < 16; j++) { o[j][0] *= c_lo; o[j][1] *= c_lo; }
+                if (HI) {
+                    const float mn_hi = fmaxf(m_hi, mx_hi);
+                    const float c_hi = ex2(m_hi - mn_hi);
+                    m_hi = mn_hi;
+                    l_hi *= c_hi;
+#pragma unroll
+                    for (int j = 0; j < 16; j++) { o[j][2] *= c_hi; o[j][3] *= c_hi; }
+                }
+            }
+            const float p00 = ex2(sc[0][0] - m_lo), p01 = ex2(sc[0][1] - m_lo);
+            const float p10 = ex2(sc[1][0] - m_lo), p11 = ex2(sc[1][1] - m_lo);
+            l_lo += (p00 + p01) + (p10 + p11);
+            const uint32_t pa0 = pack_half2(p00, p01), pa2 = pack_half2(p10, p11);
+            uint32_t pa1 = 0u, pa3 = 0u;
+            if (HI) {
+                const float q00 = ex2(sc[0][2] - m_hi), q01 = ex2(sc[0][3] - m_hi);
+                const float q10 = ex2(sc[1][2] - m_hi), q11 = ex2(sc[1][3] - m_hi);
+                l_hi += (q00 + q01) + (q10 + q11);
+                pa1 = pack_half2(q00, q01);
+                pa3 = pack_half2(q10, q11);
+            }
+#pragma unroll
+            for (int jj = 0; jj < 8; jj++) {
+                uint32_t v0, v1, v2, v3;
+                ldmatrix_x4_trans(vb + tile_off(v_key, 2 * jj + v_hi), v0, v1, v2, v3);
+                mma_16816(o[2 * jj], pa0, pa1, pa2, pa3, v0, v1);
+                mma_16816(o[2 * jj + 1], pa0, pa1, pa2, pa3, v2, v3);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[s]);
+        }
+
+        l_lo += __shfl_xor_sync(0xffffffffu, l_lo, 1);
+        l_lo += __shfl_xor_sync(0xffffffffu, l_lo, 2);
+        if (HI) {
+            l_hi += __shfl_xor_sync(0xffffffffu, l_hi, 1);
+            l_hi += __shfl_xor_sync(0xffffffffu, l_hi, 2);
+        }
+        if (!ok) { m_lo = m_hi = -INFINITY; l_lo = l_hi = 0.f; }
+        if (t == 0) {
+            m_red[warp * 16 + g] = m_lo;
+            l_red[warp * 16 + g] = l_lo;
+            if (HI) {
+                m_red[warp * 16 + g + 8] = m_hi;
+                l_red[warp * 16 + g + 8] = l_hi;
+            }
+        }
+    }
+    // All consumers are done with the ring and the producer has seen every copy land:
+    // the ring can hold the per-warp O states.
+    __syncthreads();
+    if (warp < CONSUMERS) {
+        float* ost = reinterpret_cast<float*>(ring);   // [CONSUMERS][G][128]
+        if (g < G) {
+#pragma unroll
+            for (int j = 0; j < 16; j++) {
+                float* dst = ost + ((size_t)warp * G + g) * D + 8 * j + 2 * t;
+                dst[0] = o[j][0];
+                dst[1] = o[j][1];
+            }
+        }
+        if (HI && g + 8 < G) {
+#pragma unroll
+            for (int j = 0; j < 16; j++) {
+                float* dst = ost + ((size_t)warp * G + g + 8) * D + 8 * j + 2 * t;
+                dst[0] = o[j][2];
+                dst[1] = o[j][3];
+            }
+        }
+    }
+    __syncthreads();
+
+    // ---------------------------------------------------------------- merge the 4 warps
+    const float* ost = reinterpret_cast<const float*>(ring);
+    for (int idx = threadIdx.x; idx < G * D; idx += THREADS) {
+        const int gq = idx / D, d = idx - gq * D;
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < CONSUMERS; w++) M = fmaxf(M, m_red[w * 16 + gq]);
+        float L = 0.f, O = 0.f;
+        if (M != -INFINITY) {
+#pragma unroll
+            for (int w = 0; w < CONSUMERS; w++) {
+                const float sw = ex2(m_red[w * 16 + gq] - M);
+                L += l_red[w * 16 + gq] * sw;
+                O += ost[((size_t)w * G + gq) * D + d] * sw;
+            }
+        }
+        const bool has = L > 0.f;
+        const float val = has ? O / L : 0.f;
+        const float lse_v = has ? (M + lg2(L)) * LN2 : -INFINITY;
+        const size_t row = (size_t)b * a.Hq + (size_t)kvh * G + gq;
+        if (a.direct) {
+            a.out[row * D + d] = __float2half_rn(val);
+            if (d == 0) a.lse[row] = lse_v;
+        } else {
+            const size_t slot = row * a.part_stride + a.chunk_base + chunk;
+            a.part_o[slot * D + d] = val;
+            if (d == 0) a.part_lse[slot] = lse_v;
+        }
+    }
+}
+
+// LSE merge: one warp per (sequence, q head) row, 4 dims per lane (16-byte loads).
+__global__ void __launch_bounds__(256)
+merge_states_kernel(const float* __restrict__ part_o, const float* __restrict__ part_lse,
+                    __half* __restrict__ out, float* __restrict__ lse_out, int rows, int slots) {
+    const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (row >= rows) return;
+    const float* L = part_lse + (size_t)row * slots;
+    float m = -INFINITY;
+    for (int c = lane; c < slots; c += 32) m = fmaxf(m, L[c]);
+    m = warp_max(m);
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    float wsum = 0.f;
+    if (m != -INFINITY) {
+        const float4* po = reinterpret_cast<const float4*>(part_o + (size_t)row * slots * D) + lane;
+#pragma unroll 4
+        for (int c = 0; c < slots; c++) {
+            const float w = ex2((L[c] - m) * LOG2E);
+            const float4 v = po[(size_t)c * (D / 4)];
+            wsum += w;
+            acc.x += w * v.x;
+            acc.y += w * v.y;
+            acc.z += w * v.z;
+            acc.w += w * v.w;
+        }
+    }
+    const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
+    __half2 h0 = __floats2half2_rn(acc.x * inv, acc.y * inv);
+    __half2 h1 = __floats2half2_rn(acc.z * inv, acc.w * inv);
+    uint2 pk;
+    pk.x = *reinterpret_cast<uint32_t*>(&h0);
+    pk.y = *reinterpret_cast<uint32_t*>(&h1);
+    reinterpret_cast<uint2*>(out + (size_t)row * D)[lane] = pk;
+    if (lane == 0) lse_out[row] = wsum > 0.f ? m + logf(wsum) : -INFINITY;
+}
+
+template <int G>
+const void* kernel_for() { return reinterpret_cast<const void*>(decode_partial_kernel<G>); }
+
+const void* pick(int G) {
+    switch (G) {
+        case 1: return kernel_for<1>();
+        case 2: return kernel_for<2>();
+        case 4: return kernel_for<4>();
+        case 8: return kernel_for<8>();
+        case 16: return kernel_for<16>();
+    }
+    return nullptr;
+}
+
+// Opt every partial kernel into its dynamic shared memory once per device, and record the
+// resident CTAs per SM of each (used by the split heuristic).
+struct KernelSetup {
+    int per_sm[17] = {0};
+    ckl_status st = CKL_OK;
+};
+const KernelSetup* setup(const DeviceInfo* di) {
+    static KernelSetup ks[64];
+    static std::once_flag once[64];
+    std::call_once(once[di->device], [di] {
+        KernelSetup& k = ks[di->device];
+        for (int G : {1, 2, 4, 8, 16}) {
+            const void* fn = pick(G);
+            cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+            if (e == cudaSuccess)
+                e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&k.per_sm[G], fn, THREADS, SMEM_BYTES);
+            if (e != cudaSuccess) {
+                k.st = cuda_status(e, "decode kernel setup");
+                return;
+            }
+        }
+    });
+    return &ks[di->device];
+}
+
+ckl_status validate(const ckl_decode_params* p, int* G) {
+    if (!p) return fail(CKL_INVALID_ARG, "params is NULL");
+    if (p->B < 0 || p->Hq <= 0 || p->Hkv <= 0 || p->Hq % p->Hkv)
+        return fail(CKL_INVALID_ARG, "bad head counts B=%d Hq=%d Hkv=%d", p->B, p->Hq, p->Hkv);
+    *G = p->Hq / p->Hkv;
+    if (!pick(*G)) return fail(CKL_UNSUPPORTED_SHAPE, "unsupported GQA group size %d", *G);
+    if (p->B == 0) return CKL_OK;
+    if (!p->q || !p->k_cache || !p->v_cache || !p->kv_indptr || !p->kv_indices || !p->kv_last_page_len)
+        return fail(CKL_INVALID_ARG, "NULL tensor pointer");
+    if (((uintptr_t)p->k_cache | (uintptr_t)p->v_cache) & 15)
+        return fail(CKL_INVALID_ARG, "k_cache/v_cache must be 16-byte aligned");
+    if ((uintptr_t)p->q & 3) return fail(CKL_INVALID_ARG, "q must be 4-byte aligned");
+    if (p->num_pages <= 0) return fail(CKL_INVALID_ARG, "num_pages must be > 0");
+    if (p->num_chunks <= 0 || p->chunk_tokens <= 0 || p->chunk_tokens % PAGE)
+        return fail(CKL_INVALID_ARG, "num_chunks=%d chunk_tokens=%d (must be >0, multiple of 16)",
+                    p->num_chunks, p->chunk_tokens);
+    if (p->kv_start < 0 || p->kv_start % PAGE)
+        return fail(CKL_INVALID_ARG, "kv_start=%d must be a non-negative multiple of 16", p->kv_start);
+    if (p->chunk_base < 0 || p->part_stride < p->chunk_base + p->num_chunks)
+        return fail(CKL_INVALID_ARG, "part_stride=%d < chunk_base=%d + num_chunks=%d",
+                    p->part_stride, p->chunk_base, p->num_chunks);
+    if ((long long)p->B * p->Hkv > 0x7fffffffLL || p->num_chunks > 65535)
+        return fail(CKL_UNSUPPORTED_SHAPE, "grid too large");
+    return CKL_OK;
+}
+
+ckl_status launch_partial(const ckl_decode_params* p, int G, bool direct, __half* out,
+                          float* lse, float* part_o, float* part_lse, cudaStream_t stream) {
+    const DeviceInfo* di = device_info();
+    if (!di) return CKL_CUDA_ERROR;
+    const KernelSetup* ks = setup(di);
+    if (ks->st != CKL_OK) return ks->st;
+
+    CUtensorMap tmK, tmV;
+    const uint64_t dims[4] = {(uint64_t)D, (uint64_t)p->Hkv, (uint64_t)PAGE, (uint64_t)p->num_pages};
+    const uint64_t strides[3] = {(uint64_t)D * 2, (uint64_t)p->Hkv * D * 2,
+                                 (uint64_t)PAGE * p->Hkv * D * 2};
+    const uint32_t box[4] = {64, 1, (uint32_t)PAGE, 1};
+    ckl_status st = encode_tiled(&tmK, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4,
+                                 const_cast<void*>(p->k_cache), dims, strides, box,
+                                 CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st != CKL_OK) return st;
+    st = encode_tiled(&tmV, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(p->v_cache),
+                      dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st != CKL_OK) return st;
+
+    Args a;
+    a.q = static_cast<const __half*>(p->q);
+    a.indptr = p->kv_indptr;
+    a.indices = p->kv_indices;
+    a.last = p->kv_last_page_len;
+    a.part_o = part_o;
+    a.part_lse = part_lse;
+    a.out = out;
+    a.lse = lse;
+    a.err = di->err_word;
+    a.timeout_ns = spin_timeout_ns();
+    a.B = p->B;
+    a.Hq = p->Hq;
+    a.Hkv = p->Hkv;
+    a.chunk_tokens = p->chunk_tokens;
+    a.kv_start = p->kv_start;
+    a.chunk_base = p->chunk_base;
+    a.part_stride = p->part_stride;
+    a.direct = direct ? 1 : 0;
+    a.scale_log2 = p->sm_scale * LOG2E;
+
+    void* args[] = {&tmK, &tmV, &a};
+    dim3 grid((unsigned)(p->B * p->Hkv), (unsigned)p->num_chunks);
+    CKL_CUDA_TRY(cudaLaunchKernel(pick(G), grid, dim3(THREADS), args, SMEM_BYTES, stream));
+    return CKL_OK;
+}
+
+size_t part_o_bytes(const ckl_decode_params* p) {
+    return align_up((size_t)p->B * p->Hq * p->part_stride * D * sizeof(float), 256);
+}
+
+}  // namespace attn
+}  // namespace ckl
+
+using namespace ckl;
+using namespace ckl::attn;
+
+extern "C" {
+
+ckl_status ckl_decode_plan(int G, int B, int Hkv, int max_len, int force_chunks,
+                           int* num_chunks, int* chunk_tokens) {
+    if (!num_chunks || !chunk_tokens || B <= 0 || Hkv <= 0 || max_len < 0)
+        return fail(CKL_INVALID_ARG, "decode_plan: bad arguments");
+    if (!pick(G)) return fail(CKL_UNSUPPORTED_SHAPE, "unsupported GQA group size %d", G);
+    if (max_len == 0) {
+        *num_chunks = 1;
+        *chunk_tokens = 32;
+        return CKL_OK;
+    }
+    int chunks;
+    if (force_chunks > 0) {
+        chunks = force_chunks;
+    } else {
+        const DeviceInfo* di = device_info();
+        if (!di) return CKL_CUDA_ERROR;
+        const KernelSetup* ks = setup(di);
+        if (ks->st != CKL_OK) return ks->st;
+        // Round DOWN to at most one wave of resident CTAs; chunks of >= 256 tokens.
+        const long long slots = (long long)di->sms * ks->per_sm[G];
+        const int want = (int)std::max(1LL, slots / ((long long)B * Hkv));
+        const int cap = std::max(1, ceil_div(max_len, 256));
+        chunks = std::min(want, cap);
+    }
+    const int tokens = ceil_div(ceil_div(max_len, chunks), 32) * 32;
+    *chunk_tokens = tokens;
+    *num_chunks = ceil_div(max_len, tokens);
+    return CKL_OK;
+}
+
+size_t ckl_decode_workspace_size(const ckl_decode_params* p) {
+    if (!p || p->B <= 0) return 0;
+    if (p->num_chunks == 1 && p->chunk_base == 0 && p->part_stride == 1) return 0;
+    return part_o_bytes(p) + align_up((size_t)p->B * p->Hq * p->part_stride * sizeof(float), 256);
+}
+
+ckl_status ckl_decode_partial(const ckl_decode_params* p, void* stream) {
+    int G = 0;
+    ckl_status st = validate(p, &G);
+    if (st != CKL_OK || p->B == 0) return st;
+    if (!p->part_o || !p->part_lse) return fail(CKL_INVALID_ARG, "part_o/part_lse are NULL");
+    return launch_partial(p, G, false, nullptr, nullptr, p->part_o, p->part_lse,
+                          (cudaStream_t)stream);
+}
+
+ckl_status ckl_merge_states(const float* part_o, const float* part_lse, void* out, float* lse,
+                            int rows, int num_slots, void* stream) {
+    if (rows < 0 || num_slots <= 0) return fail(CKL_INVALID_ARG, "merge_states: rows/slots");
+    if (rows == 0) return CKL_OK;
+    if (!part_o || !part_lse || !out || !lse) return fail(CKL_INVALID_ARG, "merge_states: NULL");
+    if (((uintptr_t)part_o & 15) || ((uintptr_t)out & 7))
+        return fail(CKL_INVALID_ARG, "merge_states: part_o 16-byte / out 8-byte alignment");
+    merge_states_kernel<<<ceil_div(rows, 8), 256, 0, (cudaStream_t)stream>>>(
+        part_o, part_lse, static_cast<__half*>(out), lse, rows, num_slots);
+    CKL_CUDA_TRY(cudaGetLastError());
+    return CKL_OK;
+}
+
+ckl_status ckl_decode_attention(const ckl_decode_params* p, void* out, float* lse,
+                                void* workspace, size_t workspace_bytes, void* stream) {
+    int G = 0;
+    ckl_status st = validate(p, &G);
+    if (st != CKL_OK || p->B == 0) return st;
+    if (!out || !lse) return fail(CKL_INVALID_ARG, "out/lse are NULL");
+    const cudaStream_t s = (cudaStream_t)stream;
+    if (p->num_chunks == 1 && p->chunk_base == 0 && p->part_stride == 1)
+        return launch_partial(p, G, true, static_cast<__half*>(out), lse, nullptr, nullptr, s);
+    const size_t need = ckl_decode_workspace_size(p);
+    if (!workspace || workspace_bytes < need)
+        return fail(CKL_WORKSPACE_TOO_SMALL, "decode_attention needs %zu workspace bytes, got %zu",
+                    need, workspace_bytes);
+    if ((uintptr_t)workspace & 255) return fail(CKL_INVALID_ARG, "workspace must be 256-byte aligned");
+    float* part_o = static_cast<float*>(workspace);
+    float* part_lse = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + part_o_bytes(p));
+    st = launch_partial(p, G, false, nullptr, nullptr, part_o, part_lse, s);
+    if (st != CKL_OK) return st;
+    return ckl_merge_states(part_o, part_lse, out, lse, p->B * p->Hq, p->part_stride, stream);
+}
+
+ckl_status ckl_validate_page_table(const int* h_indptr, const int* h_indices,
+                                   const int* h_last_page_len, int B, int num_pages) {
+    if (B < 0 || !h_indptr || (B > 0 && !h_last_page_len))
+        return fail(CKL_INVALID_ARG, "validate_page_table: NULL arrays");
+    if (h_indptr[0] != 0) return fail(CKL_INVALID_ARG, "kv_indptr[0] = %d, expected 0", h_indptr[0]);
+    for (int b = 0; b < B; b++) {
+        const int np = h_indptr[b + 1] - h_indptr[b];
+        if (np < 0) return fail(CKL_INVALID_ARG, "kv_indptr decreases at %d", b);
+        if (np > 0 && (h_last_page_len[b] < 1 || h_last_page_len[b] > PAGE))
+            return fail(CKL_INVALID_ARG, "kv_last_page_len[%d] = %d outside [1,16]", b,
+                        h_last_page_len[b]);
+    }
+    if (h_indptr[B] > 0 && !h_indices) return fail(CKL_INVALID_ARG, "kv_indices is NULL");
+    for (int i = 0; i < h_indptr[B]; i++)
+        if (h_indices[i] < 0 || h_indices[i] >= num_pages)
+            return fail(CKL_INVALID_ARG, "kv_indices[%d] = %d outside [0,%d)", i, h_indices[i], num_pages);
+    return CKL_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,141 @@
+/* ckl.h -- C ABI of the B200-native (sm_100a) decode layer.
+ *
+ * Drop-in boundary for the hot path of qilem/cuda-kernel-lab: paged split-KV GQA decode
+ * attention with its log-sum-exp merge, the shared-prefix cascade path, and the
+ * weight-only W4A16/W8A16 MoE expert layer. The reference exposes this path as C++ free
+ * functions and structs inside its .cu files; every entry point below names the
+ * reference function it replaces (file:line, relative to the reference project root).
+ *
+ * Conventions
+ *   - All tensors are device pointers owned by the caller; fp16 tensors are passed as
+ *     void* (IEEE binary16), fp32 as float*, indices as int32.
+ *   - `stream` is a cudaStream_t (NULL = legacy default stream). Calls are asynchronous on
+ *     it and never synchronise the host, except where a comment says "host".
+ *   - The library never allocates device memory inside a call: every scratch buffer is a
+ *     caller-provided workspace whose size a *_workspace_size() query returns. (The
+ *     reference grows a hidden cudaMalloc'd Workspace: 01_decode_attention.cu:314-331.)
+ *   - Errors are returned as ckl_status; nothing exits or aborts (the reference calls
+ *     exit(1): common/bench.cuh:21-29). ckl_last_error_string() describes the last
+ *     failure on the calling host thread.
+ *   - Layouts are the reference's: q [B,Hq,128]; K/V pages [num_pages,16,Hkv,128] (NHD);
+ *     FlashInfer-style CSR page table kv_indptr[B+1], kv_indices[nnz],
+ *     kv_last_page_len[B] (1..16); out [B,Hq,128] fp16; lse [B,Hq] fp32 natural log.
+ */
+#ifndef CKL_H_
+#define CKL_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define CKL_API __attribute__((visibility("default")))
+#else
+#define CKL_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum ckl_status {
+    CKL_OK = 0,
+    CKL_INVALID_ARG = 1,
+    CKL_UNSUPPORTED_SHAPE = 2,
+    CKL_CUDA_ERROR = 3,
+    CKL_NCCL_ERROR = 4,
+    CKL_TIMEOUT = 5,
+    CKL_WORKSPACE_TOO_SMALL = 6
+} ckl_status;
+
+/* Head size and page size of the path (01_decode_attention.cu:45-46). */
+#define CKL_HEAD_DIM 128
+#define CKL_PAGE_SIZE 16
+
+/* Description of the last failed call on this host thread ("" if none). */
+CKL_API const char* ckl_last_error_string(void);
+
+/* Library version string. */
+CKL_API const char* ckl_version(void);
+
+/* Reads and clears the device-side error word that bounded waits inside the kernels set
+ * when they give up (host; synchronises the current device). Returns CKL_TIMEOUT if a
+ * kernel launched since the last call timed out waiting on a barrier, else CKL_OK. */
+CKL_API ckl_status ckl_check_device_error(void);
+
+/* Upper bound, in nanoseconds, on any single spin-wait inside the library's kernels
+ * (default 1e9; the CKL_SPIN_TIMEOUT_NS environment variable overrides it at load). */
+CKL_API void ckl_set_spin_timeout_ns(uint64_t ns);
+
+/* ======================================================================================
+ * Paged split-KV decode attention
+ * ==================================================================================== */
+
+/* Launch descriptor; mirrors DecodeParams field for field (01_decode_attention.cu:51-65),
+ * plus num_pages (the page count of k_cache/v_cache, bounds of the TMA descriptors: a page
+ * id outside [0, num_pages) reads zeros instead of faulting). */
+typedef struct ckl_decode_params {
+    const void* q;                 /* [B, Hq, 128] fp16 */
+    const void* k_cache;           /* [num_pages, 16, Hkv, 128] fp16, 16-byte aligned */
+    const void* v_cache;           /* same layout as k_cache */
+    const int* kv_indptr;          /* [B+1] */
+    const int* kv_indices;         /* [kv_indptr[B]] physical page ids */
+    const int* kv_last_page_len;   /* [B], 1..16 */
+    float* part_o;                 /* [B*Hq, part_stride, 128] normalised partial outputs */
+    float* part_lse;               /* [B*Hq, part_stride] */
+    int B, Hq, Hkv, num_chunks, chunk_tokens;
+    int kv_start;                  /* tokens skipped at the start of every sequence */
+    int chunk_base;                /* this launch writes slots [chunk_base, +num_chunks) */
+    int part_stride;               /* partial slots per (sequence, q head) */
+    float sm_scale;
+    int num_pages;
+} ckl_decode_params;
+
+/* Split heuristic of plan_chunks (01_decode_attention.cu:292-312): about one wave of
+ * resident CTAs on the current device (SMs x resident CTAs per SM of the partial kernel),
+ * never chunks shorter than 256 tokens, chunk_tokens a multiple of 32; force_chunks > 0
+ * overrides. G = Hq/Hkv. Host only. */
+CKL_API ckl_status ckl_decode_plan(int G, int B, int Hkv, int max_len, int force_chunks,
+                           int* num_chunks, int* chunk_tokens);
+
+/* Bytes of workspace ckl_decode_attention needs for these params (0 when the launch is a
+ * single chunk and writes out/lse directly). */
+CKL_API size_t ckl_decode_workspace_size(const ckl_decode_params* p);
+
+/* One launch of the partial kernel (decode_partial<G,V>, 01_decode_attention.cu:77-236):
+ * for every (chunk, sequence, kv head) the online-softmax attention of its G query heads
+ * over keys [kv_start + chunk*chunk_tokens, +chunk_tokens), written as normalised
+ * (part_o, part_lse) into slot chunk_base + chunk. Requires chunk_tokens and kv_start to
+ * be multiples of 16. Empty chunks write o = 0, lse = -inf. */
+CKL_API ckl_status ckl_decode_partial(const ckl_decode_params* p, void* stream);
+
+/* LSE merge of partial slots (merge_states, 01_decode_attention.cu:239-255):
+ * m = max lse_i, w_i = exp(lse_i - m), out = sum w_i o_i / sum w_i (fp16),
+ * lse = m + log(sum w_i); rows with no keys give out = 0, lse = -inf. rows = B*Hq. */
+CKL_API ckl_status ckl_merge_states(const float* part_o, const float* part_lse, void* out,
+                            float* lse, int rows, int num_slots, void* stream);
+
+/* decode_attention (01_decode_attention.cu:316-331): partial + merge, with part_o /
+ * part_lse carved from `workspace` (p->part_o / p->part_lse are ignored). A single-chunk
+ * launch (num_chunks == 1, chunk_base == 0, part_stride == 1) writes out/lse directly
+ * from the partial kernel and needs no workspace. */
+CKL_API ckl_status ckl_decode_attention(const ckl_decode_params* p, void* out, float* lse,
+                                void* workspace, size_t workspace_bytes, void* stream);
+
+/* Host-side validation of a page table (host arrays): indptr non-decreasing from 0,
+ * every index in [0, num_pages), last_page_len in [1,16] for non-empty sequences. */
+CKL_API ckl_status ckl_validate_page_table(const int* h_indptr, const int* h_indices,
+                                   const int* h_last_page_len, int B, int num_pages);
+
+/* ======================================================================================
+ * Measurement
+ * ==================================================================================== */
+
+/* Achievable-bandwidth probe (stream_read, 01_decode_attention.cu:257-265): reads
+ * `bytes` (a multiple of 16) once with 16-byte loads, grid = SMs x 16 x 256 threads. */
+CKL_API ckl_status ckl_stream_read(const void* buf, size_t bytes, unsigned* sink, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CKL_H_ */
