@@ -28,9 +28,7 @@ import json
 import math
 import os
 import statistics
-import subprocess
 import sys
-import tempfile
 import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
@@ -82,47 +80,67 @@ def config_of(workload, lens, n):
 
 # ------------------------------------------------------------------ clocks
 class Clocks:
-    """nvidia-smi samples during the timed region."""
-    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    """Samples SM clock and throttle reasons through NVML on a background thread during the
+    timed region (nvidia-smi's 200 ms period is longer than a decode step loop)."""
+
+    REASONS = {"hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40,
+               "sw_power_cap": 0x4}
 
     def __init__(self, gpu_index):
-        self.idx = gpu_index
-        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        import threading
+        self.samples = []
+        self.active = False
+        self.stop_flag = False
         try:
-            self.p = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
-                                       "-lms", "200", "-i", str(gpu_index)], stdout=self.f,
-                                      stderr=subprocess.DEVNULL)
-        except OSError:
-            self.p = None
+            import pynvml
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            bus = None
+            try:
+                import torch
+                bus = torch.cuda.get_device_properties(gpu_index).pci_bus_id
+            except Exception:
+                pass
+            self.h = (pynvml.nvmlDeviceGetHandleByPciBusId(bus) if bus
+                      else pynvml.nvmlDeviceGetHandleByIndex(gpu_index))
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self.nv = None
+            return
+        self.t = threading.Thread(target=self._run, daemon=True)
+        self.t.start()
+
+    def _run(self):
+        import time as _t
+        while not self.stop_flag:
+            if self.active:
+                try:
+                    mhz = self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM)
+                    rs = self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                    self.samples.append((mhz, rs))
+                except Exception:
+                    pass
+            _t.sleep(0.0005)
+
+    def start(self):
+        self.active = True
 
     def stop(self):
-        if self.p is None:
+        if self.nv is None:
             return None
-        self.p.terminate()
-        try:
-            self.p.wait(timeout=5)
-        except subprocess.TimeoutExpired:
-            self.p.kill()
-        self.f.seek(0)
-        rows = [r.split(", ") for r in self.f.read().strip().splitlines() if r.strip()]
-        os.unlink(self.f.name)
-        sm, mx, reasons = [], 0.0, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for r in rows:
-            try:
-                sm.append(float(r[1]))
-                mx = max(mx, float(r[2]))
-                for n, v in zip(names, r[5:9]):
-                    if v.strip() == "Active":
-                        reasons.add(n)
-            except (ValueError, IndexError):
-                continue
-        if not sm:
+        self.active = False
+        self.stop_flag = True
+        self.t.join(timeout=2)
+        if not self.samples:
             return None
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+        reasons = set()
+        for _, rs in self.samples:
+            for n, bit in self.REASONS.items():
+                if rs & bit:
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(m for m, _ in self.samples),
+                "sm_max_mhz": self.max_mhz, "reasons": sorted(reasons),
+                "samples": len(self.samples), "source": "NVML during the timed region"}
 
 
 # ------------------------------------------------------------------ distributed plumbing
@@ -305,13 +323,14 @@ def run_ours(args):
     clocks = Clocks(local)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier(world)
+    clocks.start()
     e0.record(stream)
     for _ in range(args.steps):
         step()
     e1.record(stream)
     barrier(world)
-    ms = e0.elapsed_time(e1) / args.steps
     clk = clocks.stop()
+    ms = e0.elapsed_time(e1) / args.steps
     ms_max = max_over_ranks(ms, world)
     ckl.check_device_error()
 
