@@ -57,6 +57,8 @@ _SIGS = {
                                    C.c_int, C.c_void_p]),
     "ckl_decode_attention": (C.c_int, [C.POINTER(DecodeParams), C.c_void_p, C.c_void_p,
                                        C.c_void_p, C.c_size_t, C.c_void_p]),
+    "ckl_decode_attention_noalloc": (C.c_int, [C.POINTER(DecodeParams), C.c_void_p,
+                                               C.c_void_p, C.c_void_p]),
     "ckl_validate_page_table": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int,
                                           C.c_int]),
     "ckl_stream_read": (C.c_int, [C.c_void_p, C.c_size_t, C.c_void_p, C.c_void_p]),
@@ -204,6 +206,16 @@ def decode_attention(q, k_cache, v_cache, kv_indptr, kv_indices, kv_last_page_le
     check(lib().ckl_decode_attention(C.byref(p), _ptr(out), _ptr(lse), _ptr(workspace),
                                      ws_bytes, _stream(stream)), "ckl_decode_attention")
     return out, lse
+
+
+NOALLOC_SCRATCH_BYTES = 16 << 20   # CKL_NOALLOC_SCRATCH_BYTES
+
+
+def decode_attention_noalloc(p: DecodeParams, out, lse, stream=None):
+    """ckl_decode_attention_noalloc: decode with the library's built-in scratch instead of a
+    caller workspace, for hosts that cannot allocate device memory (see include/ckl.h)."""
+    check(lib().ckl_decode_attention_noalloc(C.byref(p), _ptr(out), _ptr(lse), _stream(stream)),
+          "ckl_decode_attention_noalloc")
 
 
 def validate_page_table(indptr, indices, last, num_pages):

@@ -121,6 +121,27 @@ CKL_API ckl_status ckl_merge_states(const float* part_o, const float* part_lse, 
 CKL_API ckl_status ckl_decode_attention(const ckl_decode_params* p, void* out, float* lse,
                                 void* workspace, size_t workspace_bytes, void* stream);
 
+/* Size of the scratch built into the library for ckl_decode_attention_noalloc. */
+#define CKL_NOALLOC_SCRATCH_BYTES (16u << 20)
+
+/* No counterpart in the reference. ckl_decode_attention for callers that cannot allocate
+ * device memory -- e.g. a plugin whose host process has already reserved the GPU's memory
+ * in its own pool, or a decode loop that may not call cudaMalloc/cudaFree because they can
+ * synchronise the device. Instead of a caller workspace it uses a scratch array compiled
+ * into the library: CKL_NOALLOC_SCRATCH_BYTES (16 MiB) on every GPU that loads the
+ * library, kept until the process exits. Inputs and outputs are still the caller's.
+ *   - Limit: ckl_decode_workspace_size(p) must be <= CKL_NOALLOC_SCRATCH_BYTES (about
+ *     32,500 partial rows B*Hq*num_chunks); larger launches return CKL_WORKSPACE_TOO_SMALL.
+ *     chunk_base must be 0 and part_stride == num_chunks.
+ *   - The first call on a device looks up the scratch's device address (and may load the
+ *     library's device code); make that first call before any stream capture.
+ *   - All calls on a device share the one scratch and it keeps the last call's contents
+ *     (each call rewrites every slot it reads). Calls that overlap on the GPU -- two
+ *     streams, or two host threads -- race on it: serialise them.
+ *   - Allocates nothing: no cudaMalloc, cudaFree or other allocating call. */
+CKL_API ckl_status ckl_decode_attention_noalloc(const ckl_decode_params* p, void* out,
+                                                float* lse, void* stream);
+
 /* Host-side validation of a page table (host arrays): indptr non-decreasing from 0,
  * every index in [0, num_pages), last_page_len in [1,16] for non-empty sequences. */
 CKL_API ckl_status ckl_validate_page_table(const int* h_indptr, const int* h_indices,
