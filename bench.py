@@ -53,6 +53,8 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="256x4096")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="skip the config-2 sweep and config-3 cascade rows")
     return ap.parse_args()
 
 
@@ -96,12 +98,15 @@ class Clocks:
             pynvml.nvmlInit()
             self.nv = pynvml
             bus = None
-            try:
+            try:   # NVML wants the "DDDDDDDD:BB:DD.0" string, torch gives the numbers
                 import torch
-                bus = torch.cuda.get_device_properties(gpu_index).pci_bus_id
+                pr = torch.cuda.get_device_properties(gpu_index)
+                ids = (pr.pci_domain_id, pr.pci_bus_id, pr.pci_device_id)
+                if all(isinstance(x, int) for x in ids):
+                    bus = "%08X:%02X:%02X.0" % ids
             except Exception:
-                pass
-            self.h = (pynvml.nvmlDeviceGetHandleByPciBusId(bus) if bus
+                bus = None
+            self.h = (pynvml.nvmlDeviceGetHandleByPciBusId(bus.encode()) if bus
                       else pynvml.nvmlDeviceGetHandleByIndex(gpu_index))
             self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
         except Exception:
@@ -264,6 +269,134 @@ def run_reference(args):
     return 0
 
 
+# ------------------------------------------------------------------ extra rows (N=1)
+def _fill_uniform(t, g):
+    import torch
+    flat = t.view(-1)
+    step = 1 << 28
+    for s0 in range(0, flat.numel(), step):
+        n = min(step, flat.numel() - s0)
+        flat[s0:s0 + n] = (torch.rand(n, generator=g, device=t.device) * 2 - 1).half()
+
+
+class ColdTimer:
+    """Median CUDA-event time of fn with L2 overwritten (256 MB memset, > 2x L2) before
+    every sample, as the reference's Bench::time_cold (common/bench.cuh:111-131)."""
+
+    def __init__(self, dev):
+        import torch
+        self.flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+
+    def __call__(self, fn, iters=15, warmup=3):
+        import torch
+        for _ in range(warmup):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ts = []
+        for i in range(iters):
+            self.flush.fill_(i & 0xFF)
+            e0.record()
+            fn()
+            e1.record()
+            e1.synchronize()
+            ts.append(e0.elapsed_time(e1))
+        ts.sort()
+        return ts[len(ts) // 2]
+
+
+def paged_batch(lens, dev, seed, Lp=0):
+    """A shuffled paged batch filled U(-1,1) on the device; Lp > 0 makes every sequence share
+    its first Lp tokens' physical pages (prefix caching)."""
+    import numpy as np
+    import torch
+    lens = np.asarray(lens, np.int32)
+    B = len(lens)
+    npg = (lens + PAGE - 1) // PAGE
+    indptr = np.zeros(B + 1, np.int32)
+    indptr[1:] = np.cumsum(npg)
+    last = (lens - (npg - 1) * PAGE).astype(np.int32)
+    pp = Lp // PAGE
+    total = pp + int(np.sum(npg - pp))
+    perm = np.random.default_rng(seed).permutation(total).astype(np.int32)
+    indices = np.empty(int(indptr[-1]), np.int32)
+    nxt = pp
+    for b in range(B):
+        n = int(npg[b])
+        indices[indptr[b]:indptr[b] + pp] = perm[:pp]
+        indices[indptr[b] + pp:indptr[b] + n] = perm[nxt:nxt + n - pp]
+        nxt += n - pp
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    k = torch.empty((total, PAGE, HKV, D), dtype=torch.float16, device=dev)
+    v = torch.empty_like(k)
+    _fill_uniform(k, g)
+    _fill_uniform(v, g)
+    q = (torch.rand((B, HQ, D), generator=g, device=dev) * 2 - 1).half()
+    t = lambda a: torch.from_numpy(a).to(dev)
+    return dict(q=q, k_cache=k, v_cache=v, kv_indptr=t(indptr), kv_indices=t(indices),
+                kv_last_page_len=t(last)), (lens, indptr, indices)
+
+
+def sweep_config2(ckl, dev, timer, peak):
+    """Every config-2 shape through ckl_decode_attention, cold L2, median of 15."""
+    import torch
+    rows = {}
+    for name in ("1x32768", "8x8192", "64x1024", "256x4096", "ragged256"):
+        lens = lengths(name)
+        d, _ = paged_batch(lens, dev, seed=7)
+        nc, ct = ckl.plan_chunks(HQ // HKV, len(lens), HKV, int(lens.max()))
+        p = ckl.make_params(**d, num_chunks=nc, chunk_tokens=ct)
+        out = torch.empty_like(d["q"])
+        lse = torch.empty((len(lens), HQ), dtype=torch.float32, device=dev)
+        ws = torch.empty(max(ckl.workspace_size(p), 256), dtype=torch.uint8, device=dev)
+        ms = timer(lambda: ckl.decode_attention(**d, num_chunks=nc, chunk_tokens=ct, out=out,
+                                                lse=lse, workspace=ws))
+        gbs = algorithmic_bytes(lens) / (ms * 1e-3) / 1e9
+        rows[name] = {"ms": round(ms, 4), "GB/s": round(gbs, 1),
+                      "frac_of_measured_hbm": round(gbs / peak, 3), "chunks": nc}
+        del d, out, lse, ws
+        torch.cuda.empty_cache()
+    return rows
+
+
+def bench_cascade(ckl, dev, timer, peak):
+    """64 requests x (4096 shared + 256 private) tokens, and the ragged
+    variant (suffix U[1,1024]); cascade vs plain split-KV on the same batch, cold L2."""
+    import numpy as np
+    import torch
+    res = {}
+    for name, suffix in (("64x(4096+256)", np.full(64, 256)),
+                         ("64x(4096+U[1,1024])", np.random.default_rng(77).integers(1, 1025, 64))):
+        Lp = 4096
+        lens = (Lp + suffix).astype(np.int32)
+        d, (lens, indptr, indices) = paged_batch(lens, dev, seed=21, Lp=Lp)
+        base = ckl.make_params(**d, num_chunks=1, chunk_tokens=16)
+        cp = ckl.plan_cascade(base, indptr, indices, lens, 256)
+        assert cp.use == 1 and cp.prefix_len == Lp
+        ws = torch.empty(max(ckl.cascade_workspace_size(cp), 256), dtype=torch.uint8, device=dev)
+        out = torch.empty_like(d["q"])
+        lse = torch.empty((len(lens), HQ), dtype=torch.float32, device=dev)
+        t_cas = timer(lambda: ckl.cascade_decode(cp, out=out, lse=lse, workspace=ws))
+        o_cas = out.clone()
+        t_plain = timer(lambda: ckl.decode_attention(**d, out=out, lse=lse))
+        err = float((o_cas.float() - out.float()).abs().max())
+        naive = algorithmic_bytes(lens)
+        unique = (Lp + int(np.sum(lens - Lp))) * HKV * D * 2 * 2 + len(lens) * HQ * (D * 4 + 4)
+        bound_ms = naive / (peak * 1e9) * 1e3
+        res[name] = {"ms_cascade": round(t_cas, 4), "ms_plain_split_kv": round(t_plain, 4),
+                     "naive_bytes": naive, "unique_bytes": unique,
+                     "naive_bw_bound_ms": round(bound_ms, 4),
+                     "speedup_vs_bw_bound": round(bound_ms / t_cas, 2),
+                     "speedup_vs_plain": round(t_plain / t_cas, 2),
+                     "naive_equiv_GB/s": round(naive / (t_cas * 1e-3) / 1e9, 1),
+                     "max_abs_diff_vs_plain": err, "prefix_chunks": cp.prefix_chunks,
+                     "suffix_chunks": cp.suffix.num_chunks}
+        del d, ws, out, lse
+        torch.cuda.empty_cache()
+    return res
+
+
 # ------------------------------------------------------------------ our arm
 def run_ours(args):
     import numpy as np
@@ -393,6 +526,14 @@ def run_ours(args):
 
     peak, peak_kind = measured_peak()
     achieved = byts / (kern_ms * 1e-3) / 1e9
+    extras = {}
+    if world == 1 and not args.no_extras:
+        del k, v
+        torch.cuda.empty_cache()
+        timer = ColdTimer(dev)
+        extras["config2_sweep"] = sweep_config2(ckl, dev, timer, peak)
+        extras["config3_cascade"] = bench_cascade(ckl, dev, timer, peak)
+        extras["extras_timing"] = "cold L2 (256 MB memset before each sample), median of 15"
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline_sample(int(lens.max()), os.cpu_count() or 1)
@@ -417,6 +558,7 @@ def run_ours(args):
             "cpu_baseline": cpu,
             "clocks": clk,
         }
+        line.update(extras)
         print(json.dumps(line))
     if world > 1:
         import torch.distributed as dist

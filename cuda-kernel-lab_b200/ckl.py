@@ -41,6 +41,14 @@ class DecodeParams(C.Structure):
                 ("num_pages", C.c_int)]
 
 
+class CascadePlan(C.Structure):
+    """ckl_cascade_plan_t (mirrors CascadePlan, 01_decode_attention.cu:656-662)."""
+    _fields_ = [("use", C.c_int), ("prefix_pages", C.c_int), ("prefix_len", C.c_int),
+                ("prefix_chunks", C.c_int), ("prefix_chunk_tokens", C.c_int),
+                ("qtiles", C.c_int), ("prefix_page_ids", C.c_void_p),
+                ("suffix", DecodeParams)]
+
+
 _lib = None
 
 # name -> (restype, argtypes); every function declared in include/ckl.h
@@ -62,6 +70,14 @@ _SIGS = {
     "ckl_validate_page_table": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int,
                                           C.c_int]),
     "ckl_stream_read": (C.c_int, [C.c_void_p, C.c_size_t, C.c_void_p, C.c_void_p]),
+    "ckl_shared_prefix_pages": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int]),
+    "ckl_cascade_plan": (C.c_int, [C.POINTER(DecodeParams), C.c_void_p, C.c_void_p, C.c_void_p,
+                                   C.c_int, C.POINTER(CascadePlan)]),
+    "ckl_cascade_workspace_size": (C.c_size_t, [C.POINTER(CascadePlan)]),
+    "ckl_cascade_prefix": (C.c_int, [C.POINTER(CascadePlan), C.c_void_p, C.c_void_p,
+                                     C.c_void_p]),
+    "ckl_cascade_decode": (C.c_int, [C.POINTER(CascadePlan), C.c_void_p, C.c_void_p,
+                                     C.c_void_p, C.c_size_t, C.c_void_p]),
 }
 
 
@@ -233,3 +249,54 @@ def validate_page_table(indptr, indices, last, num_pages):
 def stream_read(buf, sink, stream=None):
     check(lib().ckl_stream_read(_ptr(buf), buf.numel() * buf.element_size(), _ptr(sink),
                                 _stream(stream)), "ckl_stream_read")
+
+
+# ------------------------------------------------------------------ cascade
+def _np_i32(a):
+    import numpy as np
+    return np.ascontiguousarray(a, dtype=np.int32)
+
+
+def shared_prefix_pages(indptr, indices):
+    """shared_prefix_pages (01_decode_attention.cu:636-646) on host int32 arrays."""
+    ip, ix = _np_i32(indptr), _np_i32(indices)
+    return lib().ckl_shared_prefix_pages(ip.ctypes.data_as(C.c_void_p),
+                                         ix.ctypes.data_as(C.c_void_p), len(ip) - 1)
+
+
+def plan_cascade(base: DecodeParams, h_indptr, h_indices, h_lens, min_prefix=256):
+    """plan_cascade (01_decode_attention.cu:666-701) from host copies of the page table."""
+    ip, ix, ln = _np_i32(h_indptr), _np_i32(h_indices), _np_i32(h_lens)
+    cp = CascadePlan()
+    check(lib().ckl_cascade_plan(C.byref(base), ip.ctypes.data_as(C.c_void_p),
+                                 ix.ctypes.data_as(C.c_void_p), ln.ctypes.data_as(C.c_void_p),
+                                 min_prefix, C.byref(cp)), "ckl_cascade_plan")
+    cp._keep = (base,)
+    return cp
+
+
+def cascade_workspace_size(cp: CascadePlan):
+    return lib().ckl_cascade_workspace_size(C.byref(cp))
+
+
+def cascade_prefix(cp: CascadePlan, part_o, part_lse, stream=None):
+    check(lib().ckl_cascade_prefix(C.byref(cp), _ptr(part_o), _ptr(part_lse), _stream(stream)),
+          "ckl_cascade_prefix")
+
+
+def cascade_decode(cp: CascadePlan, out=None, lse=None, workspace=None, stream=None):
+    """cascade_decode (01_decode_attention.cu:703-712) -> (out, lse)."""
+    torch = _torch()
+    sp = cp.suffix
+    dev = torch.device("cuda", torch.cuda.current_device())
+    if out is None:
+        out = torch.empty((sp.B, sp.Hq, HEAD_DIM), dtype=torch.float16, device=dev)
+    if lse is None:
+        lse = torch.empty((sp.B, sp.Hq), dtype=torch.float32, device=dev)
+    need = cascade_workspace_size(cp)
+    if need and (workspace is None or workspace.numel() * workspace.element_size() < need):
+        workspace = torch.empty(need, dtype=torch.uint8, device=dev)
+    ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
+    check(lib().ckl_cascade_decode(C.byref(cp), _ptr(out), _ptr(lse), _ptr(workspace), ws_bytes,
+                                   _stream(stream)), "ckl_cascade_decode")
+    return out, lse

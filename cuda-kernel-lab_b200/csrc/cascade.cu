@@ -1,0 +1,421 @@
+// cascade.cu -- shared-prefix (cascade) decode for sm_100a.
+//
+// Replaces shared_prefix_pages / plan_cascade / cascade_prefix / cascade_decode of the
+// reference (01_decode_attention.cu:446-712). When every sequence of a batch starts with
+// the same physical pages (prefix caching), the plain kernel reads those pages once per
+// sequence. The cascade reads them once per kv head:
+//
+//   1. host: the longest run of physical pages every sequence starts with (each keeps >= 1
+//      private page), from the caller's host copy of the page table;
+//   2. prefix kernel: the B*G query rows that share a kv head are stacked into 128-row tiles
+//      (8 consumer warps x 16 rows); a producer warp TMA-loads each shared page once into an
+//      8-stage ring and every consumer warp runs Q K^T and P V on it with mma.sync, with a
+//      single-pass online softmax (the reference makes two passes because WMMA cannot
+//      rescale its accumulators; register fragments can);
+//   3. suffix: the split-KV partial kernel from kv_start = prefix length;
+//   4. one LSE merge over prefix and suffix slots.
+
+#include <algorithm>
+#include <mutex>
+
+#include "attn_common.cuh"
+
+namespace ckl {
+namespace cascade {
+
+using namespace attn;
+
+constexpr int PWARPS = 8;                     // consumer warps, 16 stacked query rows each
+constexpr int PROWS = PWARPS * 16;            // query rows per CTA
+constexpr int PTHREADS = (PWARPS + 1) * 32;   // + one TMA producer warp
+constexpr int PSTAGES = 8;
+constexpr int P_RING = PSTAGES * STAGE_BYTES;
+constexpr int P_SMEM = 1024 + P_RING + 2 * PSTAGES * 8;
+
+struct PrefixArgs {
+    const __half* q;
+    const int* prefix_pages;
+    float* part_o;
+    float* part_lse;
+    unsigned* err;
+    unsigned long long timeout_ns;
+    int B, Hq, Hkv, G, prefix_len, chunk_tokens, part_stride;
+    float scale_log2;
+};
+
+// grid = (prefix chunks, ceil(B*G / 128), Hkv). Writes the normalised partial (o, lse) of
+// every stacked query row it covers into slot blockIdx.x.
+__global__ void __launch_bounds__(PTHREADS, 1)
+cascade_prefix_kernel(const __grid_constant__ CUtensorMap tmK,
+                      const __grid_constant__ CUtensorMap tmV, const PrefixArgs a) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* ring = align_ptr<1024>(smem_raw);
+    uint64_t* full = reinterpret_cast<uint64_t*>(ring + P_RING);
+    uint64_t* empty = full + PSTAGES;
+
+    const int chunk = blockIdx.x, qtile = blockIdx.y, kvh = blockIdx.z;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int kbeg = chunk * a.chunk_tokens;
+    const int kend = min(a.prefix_len, kbeg + a.chunk_tokens);
+    const int p0 = kbeg / PAGE;
+    const int npg = kend > kbeg ? (kend - kbeg + PAGE - 1) / PAGE : 0;
+    const int nq = a.B * a.G;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < PSTAGES; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], PWARPS);
+        }
+        fence_barrier_init();
+    }
+    __syncthreads();
+    const uint64_t deadline = globaltimer() + a.timeout_ns;
+
+    if (warp == PWARPS) {
+        // ---------------------------------------------------------------- producer warp
+        if (lane == 0) {
+            tma_prefetch_desc(&tmK);
+            tma_prefetch_desc(&tmV);
+        }
+        // the prefix is re-read by the other query tiles of this kv head: keep it in L2
+        const uint64_t pol = policy_evict_last();
+        int ok = 1, issued = 0;
+        for (int base = 0; base < npg && ok; base += 32) {
+            const int cnt = min(32, npg - base);
+            const int my_page = lane < cnt ? __ldg(a.prefix_pages + p0 + base + lane) : 0;
+            for (int j = 0; j < cnt; j++) {
+                const int page = __shfl_sync(0xffffffffu, my_page, j);
+                if (lane == 0) {
+                    const int i = base + j, s = i % PSTAGES;
+                    if (i >= PSTAGES) ok = mbar_wait(&empty[s], ((i / PSTAGES) - 1) & 1, deadline, a.err);
+                    if (ok) {
+                        mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
+                        load_page(ring + s * STAGE_BYTES, &tmK, &tmV, kvh, page, &full[s], pol);
+                        issued = i + 1;
+                    }
+                }
+                ok = __shfl_sync(0xffffffffu, ok, 0);
+                if (!ok) break;
+            }
+        }
+        if (lane == 0) {
+            for (int s = 0; s < PSTAGES && s < issued; s++) {
+                const int i_last = s + ((issued - 1 - s) / PSTAGES) * PSTAGES;
+                mbar_wait(&full[s], (i_last / PSTAGES) & 1, deadline, a.err);
+            }
+        }
+        return;
+    }
+
+    // -------------------------------------------------------------------- consumer warps
+    const int g = lane >> 2, t = lane & 3;
+    const int r_lo = qtile * PROWS + warp * 16 + g, r_hi = r_lo + 8;
+    const bool ok_lo = r_lo < nq, ok_hi = r_hi < nq;
+    const bool active = qtile * PROWS + warp * 16 < nq;   // warp-uniform
+    size_t qrow_lo = 0, qrow_hi = 0;
+    if (ok_lo) qrow_lo = (size_t)(r_lo / a.G) * a.Hq + (size_t)kvh * a.G + r_lo % a.G;
+    if (ok_hi) qrow_hi = (size_t)(r_hi / a.G) * a.Hq + (size_t)kvh * a.G + r_hi % a.G;
+
+    uint32_t qa0[8], qa1[8], qa2[8], qa3[8];
+#pragma unroll
+    for (int kk = 0; kk < 8; kk++) qa0[kk] = qa1[kk] = qa2[kk] = qa3[kk] = 0u;
+    if (ok_lo) {
+        const uint32_t* qr = reinterpret_cast<const uint32_t*>(a.q + qrow_lo * D);
+#pragma unroll
+        for (int kk = 0; kk < 8; kk++) {
+            qa0[kk] = __ldg(qr + 8 * kk + t);
+            qa2[kk] = __ldg(qr + 8 * kk + 4 + t);
+        }
+    }
+    if (ok_hi) {
+        const uint32_t* qr = reinterpret_cast<const uint32_t*>(a.q + qrow_hi * D);
+#pragma unroll
+        for (int kk = 0; kk < 8; kk++) {
+            qa1[kk] = __ldg(qr + 8 * kk + t);
+            qa3[kk] = __ldg(qr + 8 * kk + 4 + t);
+        }
+    }
+    float o[16][4];
+#pragma unroll
+    for (int j = 0; j < 16; j++) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+    float m_lo = -INFINITY, m_hi = -INFINITY, l_lo = 0.f, l_hi = 0.f;
+    const int k_key = (lane & 7) + ((lane >> 4) << 3), k_hi = (lane >> 3) & 1;
+    const int v_key = (lane & 7) + (((lane >> 3) & 1) << 3), v_hi = lane >> 4;
+
+    bool ok = true;
+    for (int i = 0; i < npg; i++) {
+        const int s = i % PSTAGES;
+        const bool got = mbar_wait(&full[s], (i / PSTAGES) & 1, deadline, a.err);
+        if (!__all_sync(0xffffffffu, got)) { ok = false; break; }
+        if (active) {
+            const uint32_t kb = smem_u32(ring + s * STAGE_BYTES);
+            const uint32_t vb = kb + KV_TILE;
+            float sc[2][4];
+#pragma unroll
+            for (int n = 0; n < 2; n++) sc[n][0] = sc[n][1] = sc[n][2] = sc[n][3] = 0.f;
+#pragma unroll
+            for (int kk = 0; kk < 8; kk++) {
+                uint32_t b00, b01, b10, b11;
+                ldmatrix_x4(kb + tile_off(k_key, 2 * kk + k_hi), b00, b01, b10, b11);
+                mma_16816(sc[0], qa0[kk], qa1[kk], qa2[kk], qa3[kk], b00, b01);
+                mma_16816(sc[1], qa0[kk], qa1[kk], qa2[kk], qa3[kk], b10, b11);
+            }
+            const int kbase = (p0 + i) * PAGE;
+            if (kbase + PAGE > kend) {
+#pragma unroll
+                for (int n = 0; n < 2; n++)
+#pragma unroll
+                    for (int c = 0; c < 4; c++)
+                        if (kbase + n * 8 + 2 * t + (c & 1) >= kend) sc[n][c] = -INFINITY;
+            }
+#pragma unroll
+            for (int n = 0; n < 2; n++)
+#pragma unroll
+                for (int c = 0; c < 4; c++) sc[n][c] *= a.scale_log2;
+            float mx_lo = fmaxf(fmaxf(sc[0][0], sc[0][1]), fmaxf(sc[1][0], sc[1][1]));
+            float mx_hi = fmaxf(fmaxf(sc[0][2], sc[0][3]), fmaxf(sc[1][2], sc[1][3]));
+            mx_lo = fmaxf(mx_lo, __shfl_xor_sync(0xffffffffu, mx_lo, 1));
+            mx_hi = fmaxf(mx_hi, __shfl_xor_sync(0xffffffffu, mx_hi, 1));
+            mx_lo = fmaxf(mx_lo, __shfl_xor_sync(0xffffffffu, mx_lo, 2));
+            mx_hi = fmaxf(mx_hi, __shfl_xor_sync(0xffffffffu, mx_hi, 2));
+            const bool need = mx_lo > m_lo + RESCALE_THRESHOLD || mx_hi > m_hi + RESCALE_THRESHOLD;
+            if (__any_sync(0xffffffffu, need)) {
+                const float mn_lo = fmaxf(m_lo, mx_lo), mn_hi = fmaxf(m_hi, mx_hi);
+                const float c_lo = ex2(m_lo - mn_lo), c_hi = ex2(m_hi - mn_hi);
+                m_lo = mn_lo;
+                m_hi = mn_hi;
+                l_lo *= c_lo;
+                l_hi *= c_hi;
+#pragma unroll
+                for (int j = 0; j < 16; j++) {
+                    o[j][0] *= c_lo;
+                    o[j][1] *= c_lo;
+                    o[j][2] *= c_hi;
+                    o[j][3] *= c_hi;
+                }
+            }
+            const float p00 = ex2(sc[0][0] - m_lo), p01 = ex2(sc[0][1] - m_lo);
+            const float p10 = ex2(sc[1][0] - m_lo), p11 = ex2(sc[1][1] - m_lo);
+            const float q00 = ex2(sc[0][2] - m_hi), q01 = ex2(sc[0][3] - m_hi);
+            const float q10 = ex2(sc[1][2] - m_hi), q11 = ex2(sc[1][3] - m_hi);
+            l_lo += (p00 + p01) + (p10 + p11);
+            l_hi += (q00 + q01) + (q10 + q11);
+            const uint32_t pa0 = pack_half2(p00, p01), pa2 = pack_half2(p10, p11);
+            const uint32_t pa1 = pack_half2(q00, q01), pa3 = pack_half2(q10, q11);
+#pragma unroll
+            for (int jj = 0; jj < 8; jj++) {
+                uint32_t v0, v1, v2, v3;
+                ldmatrix_x4_trans(vb + tile_off(v_key, 2 * jj + v_hi), v0, v1, v2, v3);
+                mma_16816(o[2 * jj], pa0, pa1, pa2, pa3, v0, v1);
+                mma_16816(o[2 * jj + 1], pa0, pa1, pa2, pa3, v2, v3);
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+    }
+    if (!active) return;
+
+    l_lo += __shfl_xor_sync(0xffffffffu, l_lo, 1);
+    l_lo += __shfl_xor_sync(0xffffffffu, l_lo, 2);
+    l_hi += __shfl_xor_sync(0xffffffffu, l_hi, 1);
+    l_hi += __shfl_xor_sync(0xffffffffu, l_hi, 2);
+    if (!ok) { l_lo = l_hi = 0.f; }
+    const float inv_lo = l_lo > 0.f ? 1.f / l_lo : 0.f, inv_hi = l_hi > 0.f ? 1.f / l_hi : 0.f;
+    if (ok_lo) {
+        const size_t slot = qrow_lo * a.part_stride + chunk;
+        float* dst = a.part_o + slot * D + 2 * t;
+#pragma unroll
+        for (int j = 0; j < 16; j++)
+            *reinterpret_cast<float2*>(dst + 8 * j) = make_float2(o[j][0] * inv_lo, o[j][1] * inv_lo);
+        if (t == 0) a.part_lse[slot] = l_lo > 0.f ? (m_lo + lg2(l_lo)) * LN2 : -INFINITY;
+    }
+    if (ok_hi) {
+        const size_t slot = qrow_hi * a.part_stride + chunk;
+        float* dst = a.part_o + slot * D + 2 * t;
+#pragma unroll
+        for (int j = 0; j < 16; j++)
+            *reinterpret_cast<float2*>(dst + 8 * j) = make_float2(o[j][2] * inv_hi, o[j][3] * inv_hi);
+        if (t == 0) a.part_lse[slot] = l_hi > 0.f ? (m_hi + lg2(l_hi)) * LN2 : -INFINITY;
+    }
+}
+
+struct PrefixSetup {
+    int per_sm = 0;
+    ckl_status st = CKL_OK;
+};
+const PrefixSetup* setup(const DeviceInfo* di) {
+    static PrefixSetup ps[64];
+    static std::once_flag once[64];
+    std::call_once(once[di->device], [di] {
+        PrefixSetup& p = ps[di->device];
+        const void* fn = reinterpret_cast<const void*>(cascade_prefix_kernel);
+        cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, P_SMEM);
+        if (e == cudaSuccess)
+            e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&p.per_sm, fn, PTHREADS, P_SMEM);
+        if (e != cudaSuccess) p.st = cuda_status(e, "cascade prefix kernel setup");
+    });
+    return &ps[di->device];
+}
+
+ckl_status launch_prefix(const ckl_cascade_plan_t* cp, float* part_o, float* part_lse,
+                         cudaStream_t stream) {
+    const ckl_decode_params& b = cp->suffix;
+    const DeviceInfo* di = device_info();
+    if (!di) return CKL_CUDA_ERROR;
+    const PrefixSetup* ps = setup(di);
+    if (ps->st != CKL_OK) return ps->st;
+    CUtensorMap tmK, tmV;
+    ckl_status st = encode_kv_maps(b.k_cache, b.v_cache, b.Hkv, b.num_pages, &tmK, &tmV);
+    if (st != CKL_OK) return st;
+    PrefixArgs a;
+    a.q = static_cast<const __half*>(b.q);
+    a.prefix_pages = cp->prefix_page_ids;
+    a.part_o = part_o;
+    a.part_lse = part_lse;
+    a.err = di->err_word;
+    a.timeout_ns = spin_timeout_ns();
+    a.B = b.B;
+    a.Hq = b.Hq;
+    a.Hkv = b.Hkv;
+    a.G = b.Hq / b.Hkv;
+    a.prefix_len = cp->prefix_len;
+    a.chunk_tokens = cp->prefix_chunk_tokens;
+    a.part_stride = b.part_stride;
+    a.scale_log2 = b.sm_scale * LOG2E;
+    void* args[] = {&tmK, &tmV, &a};
+    dim3 grid((unsigned)cp->prefix_chunks, (unsigned)cp->qtiles, (unsigned)b.Hkv);
+    CKL_CUDA_TRY(cudaLaunchKernel(reinterpret_cast<const void*>(cascade_prefix_kernel), grid,
+                                  dim3(PTHREADS), args, P_SMEM, stream));
+    return CKL_OK;
+}
+
+ckl_status check_plan(const ckl_cascade_plan_t* cp) {
+    if (!cp) return fail(CKL_INVALID_ARG, "cascade plan is NULL");
+    if (!cp->use) return CKL_OK;
+    if (!cp->prefix_page_ids || cp->prefix_len <= 0 || cp->prefix_len % PAGE ||
+        cp->prefix_chunks <= 0 || cp->prefix_chunk_tokens <= 0 || cp->prefix_chunk_tokens % PAGE ||
+        cp->qtiles <= 0 || cp->suffix.chunk_base != cp->prefix_chunks ||
+        cp->suffix.kv_start != cp->prefix_len)
+        return fail(CKL_INVALID_ARG, "inconsistent cascade plan");
+    if ((long long)cp->qtiles * PROWS < (long long)cp->suffix.B * (cp->suffix.Hq / cp->suffix.Hkv))
+        return fail(CKL_INVALID_ARG, "cascade plan: qtiles do not cover B*G query rows");
+    if (cp->prefix_chunks > 0x7fffffff / 1 || cp->qtiles > 65535 || cp->suffix.Hkv > 65535)
+        return fail(CKL_UNSUPPORTED_SHAPE, "cascade grid too large");
+    return CKL_OK;
+}
+
+}  // namespace cascade
+}  // namespace ckl
+
+using namespace ckl;
+using namespace ckl::cascade;
+
+extern "C" {
+
+int ckl_shared_prefix_pages(const int* h_indptr, const int* h_indices, int B) {
+    if (!h_indptr || B < 2 || !h_indices) return 0;
+    for (int P = 0;; P++) {
+        for (int b = 0; b < B; b++)
+            if (P >= h_indptr[b + 1] - h_indptr[b] - 1) return P;
+        const int pg = h_indices[h_indptr[0] + P];
+        for (int b = 1; b < B; b++)
+            if (h_indices[h_indptr[b] + P] != pg) return P;
+    }
+}
+
+ckl_status ckl_cascade_plan(const ckl_decode_params* base, const int* h_indptr,
+                            const int* h_indices, const int* h_lens, int min_prefix,
+                            ckl_cascade_plan_t* plan) {
+    if (!plan || !base || !h_indptr || !h_lens) return fail(CKL_INVALID_ARG, "cascade_plan: NULL");
+    int G = 0;
+    ckl_status st = attn::validate(base, &G);
+    if (st != CKL_OK) return st;
+    *plan = ckl_cascade_plan_t{};
+    plan->suffix = *base;
+    int max_len = 0;
+    for (int b = 0; b < base->B; b++) max_len = std::max(max_len, h_lens[b]);
+    const int pages = ckl_shared_prefix_pages(h_indptr, h_indices, base->B);
+    const int Lp = pages * PAGE;
+    if (Lp == 0 || Lp < min_prefix) {
+        // no usable shared prefix: the plan is the plain split-KV decode
+        plan->use = 0;
+        st = ckl_decode_plan(G, base->B, base->Hkv, max_len, 0, &plan->suffix.num_chunks,
+                             &plan->suffix.chunk_tokens);
+        plan->suffix.kv_start = 0;
+        plan->suffix.chunk_base = 0;
+        plan->suffix.part_stride = plan->suffix.num_chunks;
+        return st;
+    }
+    const DeviceInfo* di = device_info();
+    if (!di) return CKL_CUDA_ERROR;
+    const PrefixSetup* ps = setup(di);
+    if (ps->st != CKL_OK) return ps->st;
+    plan->use = 1;
+    plan->prefix_pages = pages;
+    plan->prefix_len = Lp;
+    plan->qtiles = ceil_div(base->B * G, PROWS);
+    // about one wave of prefix CTAs, chunks of >= 256 tokens, a multiple of 32 tokens
+    int cpre = std::max(1, di->sms * std::max(1, ps->per_sm) / (plan->qtiles * base->Hkv));
+    cpre = std::min(cpre, std::max(1, Lp / 256));
+    const int ctok = ceil_div(ceil_div(Lp, cpre), 32) * 32;
+    plan->prefix_chunks = ceil_div(Lp, ctok);
+    plan->prefix_chunk_tokens = ctok;
+    plan->prefix_page_ids = base->kv_indices + h_indptr[0];
+    int max_suffix = 0;
+    for (int b = 0; b < base->B; b++) max_suffix = std::max(max_suffix, h_lens[b] - Lp);
+    st = ckl_decode_plan(G, base->B, base->Hkv, std::max(max_suffix, 1), 0,
+                         &plan->suffix.num_chunks, &plan->suffix.chunk_tokens);
+    if (st != CKL_OK) return st;
+    plan->suffix.kv_start = Lp;
+    plan->suffix.chunk_base = plan->prefix_chunks;
+    plan->suffix.part_stride = plan->prefix_chunks + plan->suffix.num_chunks;
+    return CKL_OK;
+}
+
+size_t ckl_cascade_workspace_size(const ckl_cascade_plan_t* plan) {
+    if (!plan) return 0;
+    if (!plan->use) return ckl_decode_workspace_size(&plan->suffix);
+    const ckl_decode_params& s = plan->suffix;
+    return attn::part_o_bytes(&s) + align_up((size_t)s.B * s.Hq * s.part_stride * sizeof(float), 256);
+}
+
+ckl_status ckl_cascade_prefix(const ckl_cascade_plan_t* plan, float* part_o, float* part_lse,
+                              void* stream) {
+    ckl_status st = check_plan(plan);
+    if (st != CKL_OK) return st;
+    if (!plan->use) return fail(CKL_INVALID_ARG, "cascade_prefix: plan has no shared prefix");
+    int G = 0;
+    st = attn::validate(&plan->suffix, &G);
+    if (st != CKL_OK || plan->suffix.B == 0) return st;
+    if (!part_o || !part_lse) return fail(CKL_INVALID_ARG, "cascade_prefix: NULL partials");
+    return launch_prefix(plan, part_o, part_lse, (cudaStream_t)stream);
+}
+
+ckl_status ckl_cascade_decode(const ckl_cascade_plan_t* plan, void* out, float* lse,
+                              void* workspace, size_t workspace_bytes, void* stream) {
+    ckl_status st = check_plan(plan);
+    if (st != CKL_OK) return st;
+    if (!plan->use)
+        return ckl_decode_attention(&plan->suffix, out, lse, workspace, workspace_bytes, stream);
+    int G = 0;
+    st = attn::validate(&plan->suffix, &G);
+    if (st != CKL_OK || plan->suffix.B == 0) return st;
+    if (!out || !lse) return fail(CKL_INVALID_ARG, "cascade_decode: out/lse are NULL");
+    const size_t need = ckl_cascade_workspace_size(plan);
+    if (!workspace || workspace_bytes < need)
+        return fail(CKL_WORKSPACE_TOO_SMALL, "cascade_decode needs %zu workspace bytes, got %zu",
+                    need, workspace_bytes);
+    if ((uintptr_t)workspace & 255) return fail(CKL_INVALID_ARG, "workspace must be 256-byte aligned");
+    const cudaStream_t s = (cudaStream_t)stream;
+    float* part_o = static_cast<float*>(workspace);
+    float* part_lse = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) +
+                                               attn::part_o_bytes(&plan->suffix));
+    st = launch_prefix(plan, part_o, part_lse, s);
+    if (st != CKL_OK) return st;
+    st = attn::launch_partial(&plan->suffix, G, false, nullptr, nullptr, part_o, part_lse, s);
+    if (st != CKL_OK) return st;
+    return ckl_merge_states(part_o, part_lse, out, lse, plan->suffix.B * plan->suffix.Hq,
+                            plan->suffix.part_stride, stream);
+}
+
+}  // extern "C"

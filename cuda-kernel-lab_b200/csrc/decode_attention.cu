@@ -27,27 +27,18 @@
 #include <cstring>
 #include <mutex>
 
-#include "ckl_internal.h"
-#include "ckl_ptx.cuh"
+#include "attn_common.cuh"
 
 namespace ckl {
 namespace attn {
 
-constexpr int D = CKL_HEAD_DIM;
-constexpr int PAGE = CKL_PAGE_SIZE;
 constexpr int CONSUMERS = 4;
 constexpr int THREADS = (CONSUMERS + 1) * 32;
 constexpr int STAGES = 8;
-constexpr int HALF_TILE = PAGE * 64 * 2;  // 16 keys x 64 dims fp16 = 2 KB, 128B-swizzled
-constexpr int KV_TILE = 2 * HALF_TILE;    // one page of K (or V) for one head: 4 KB
-constexpr int STAGE_BYTES = 2 * KV_TILE;  // K + V
 constexpr int RING_BYTES = STAGES * STAGE_BYTES;
 constexpr int BAR_BYTES = 2 * STAGES * 8;
 constexpr int RED_BYTES = 2 * CONSUMERS * 16 * 4;
 constexpr int SMEM_BYTES = 1024 /*alignment slack*/ + RING_BYTES + BAR_BYTES + RED_BYTES;
-constexpr float LOG2E = 1.4426950408889634f;
-constexpr float LN2 = 0.6931471805599453f;
-constexpr float RESCALE_THRESHOLD = 8.f;   // log2 units: p may grow to 2^8 before a rescale
 
 struct Args {
     const __half* q;
@@ -63,14 +54,6 @@ struct Args {
     int B, Hq, Hkv, chunk_tokens, kv_start, chunk_base, part_stride, direct;
     float scale_log2;
 };
-
-// Byte offset of 16-byte chunk `cd` (0..15, dims 8cd..8cd+7) of key `key` inside a page
-// tile: [half = cd/8][key][64 dims] with the TMA 128B swizzle (chunk ^= key%8 within each
-// 128-byte row; the tile is 1024-byte aligned).
-__device__ __forceinline__ uint32_t tile_off(int key, int cd) {
-    const int c = cd & 7;
-    return (uint32_t)((cd >> 3) * HALF_TILE + key * 128 + ((c ^ (key & 7)) << 4));
-}
 
 template <int G>
 __global__ void __launch_bounds__(THREADS, 2)
@@ -130,12 +113,8 @@ decode_partial_kernel(const __grid_constant__ CUtensorMap tmK,
                     const int i = base + j, s = i % STAGES;
                     if (i >= STAGES) ok = mbar_wait(&empty[s], ((i / STAGES) - 1) & 1, deadline, a.err);
                     if (ok) {
-                        uint8_t* st = ring + s * STAGE_BYTES;
                         mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
-                        tma_load_4d(st, &tmK, 0, kvh, 0, page, &full[s], pol);
-                        tma_load_4d(st + HALF_TILE, &tmK, 64, kvh, 0, page, &full[s], pol);
-                        tma_load_4d(st + KV_TILE, &tmV, 0, kvh, 0, page, &full[s], pol);
-                        tma_load_4d(st + KV_TILE + HALF_TILE, &tmV, 64, kvh, 0, page, &full[s], pol);
+                        load_page(ring + s * STAGE_BYTES, &tmK, &tmV, kvh, page, &full[s], pol);
                         issued = i + 1;
                     }
                 }
@@ -443,16 +422,7 @@ ckl_status launch_partial(const ckl_decode_params* p, int G, bool direct, __half
     if (ks->st != CKL_OK) return ks->st;
 
     CUtensorMap tmK, tmV;
-    const uint64_t dims[4] = {(uint64_t)D, (uint64_t)p->Hkv, (uint64_t)PAGE, (uint64_t)p->num_pages};
-    const uint64_t strides[3] = {(uint64_t)D * 2, (uint64_t)p->Hkv * D * 2,
-                                 (uint64_t)PAGE * p->Hkv * D * 2};
-    const uint32_t box[4] = {64, 1, (uint32_t)PAGE, 1};
-    ckl_status st = encode_tiled(&tmK, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4,
-                                 const_cast<void*>(p->k_cache), dims, strides, box,
-                                 CU_TENSOR_MAP_SWIZZLE_128B);
-    if (st != CKL_OK) return st;
-    st = encode_tiled(&tmV, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(p->v_cache),
-                      dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+    ckl_status st = encode_kv_maps(p->k_cache, p->v_cache, p->Hkv, p->num_pages, &tmK, &tmV);
     if (st != CKL_OK) return st;
 
     Args a;

@@ -148,6 +148,51 @@ CKL_API ckl_status ckl_validate_page_table(const int* h_indptr, const int* h_ind
                                    const int* h_last_page_len, int B, int num_pages);
 
 /* ======================================================================================
+ * Shared-prefix (cascade) decode
+ * ==================================================================================== */
+
+/* Cascade launch plan (CascadePlan, 01_decode_attention.cu:656-662). */
+typedef struct ckl_cascade_plan_t {
+    int use;                      /* 0: no usable shared prefix; `suffix` is then the plain
+                                     split-KV plan and ckl_cascade_decode runs it */
+    int prefix_pages;             /* pages every sequence starts with */
+    int prefix_len;               /* prefix_pages * 16 tokens */
+    int prefix_chunks;            /* prefix partials occupy slots [0, prefix_chunks) */
+    int prefix_chunk_tokens;
+    int qtiles;                   /* ceil(B*G / 128) stacked-query tiles per kv head */
+    const int* prefix_page_ids;   /* device: kv_indices + kv_indptr[0] */
+    ckl_decode_params suffix;     /* kv_start = prefix_len, chunk_base = prefix_chunks,
+                                     part_stride = prefix_chunks + suffix chunks */
+} ckl_cascade_plan_t;
+
+/* shared_prefix_pages (01_decode_attention.cu:636-646): the longest run of physical pages
+ * every sequence starts with, each sequence keeping at least one private page; B < 2 -> 0.
+ * Host arrays. */
+CKL_API int ckl_shared_prefix_pages(const int* h_indptr, const int* h_indices, int B);
+
+/* plan_cascade (01_decode_attention.cu:666-701): detects the shared prefix from the host
+ * copy of the page table; use = 0 when it is shorter than min_prefix tokens (the reference
+ * default is 256). Prefix chunks fill about one wave of prefix CTAs. Host only. */
+CKL_API ckl_status ckl_cascade_plan(const ckl_decode_params* base, const int* h_indptr,
+                                    const int* h_indices, const int* h_lens, int min_prefix,
+                                    ckl_cascade_plan_t* plan);
+
+/* Workspace bytes of ckl_cascade_decode (partials of all prefix and suffix slots). */
+CKL_API size_t ckl_cascade_workspace_size(const ckl_cascade_plan_t* plan);
+
+/* The prefix kernel alone (cascade_prefix, 01_decode_attention.cu:486-632): attention of
+ * all B*G query rows of each kv head over the shared prefix, each page read once per kv
+ * head, written as partial slots [0, prefix_chunks) of part_o / part_lse (laid out with
+ * plan->suffix.part_stride slots per row). */
+CKL_API ckl_status ckl_cascade_prefix(const ckl_cascade_plan_t* plan, float* part_o,
+                                      float* part_lse, void* stream);
+
+/* cascade_decode (01_decode_attention.cu:703-712): prefix kernel, suffix partial kernel
+ * from kv_start = prefix_len, and one LSE merge over all slots. */
+CKL_API ckl_status ckl_cascade_decode(const ckl_cascade_plan_t* plan, void* out, float* lse,
+                                      void* workspace, size_t workspace_bytes, void* stream);
+
+/* ======================================================================================
  * Measurement
  * ==================================================================================== */
 
