@@ -397,6 +397,123 @@ def bench_cascade(ckl, dev, timer, peak):
     return res
 
 
+def _moe_active_bytes(q, ids_np):
+    """Algorithmic bytes of one layer step: packed weights + scales + zeros of every active
+    expert (gate, up, down) + X in + out."""
+    import numpy as np
+    active = len(np.unique(ids_np))
+    return active * sum(w.bytes_per_expert() for w in q)
+
+
+class GraphStep:
+    """The step captured once in a CUDA graph and replayed (the layer never syncs the host
+    and never allocates, so it is capturable)."""
+
+    def __init__(self, fn, dev):
+        import torch
+        s = torch.cuda.Stream(device=dev)
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            for _ in range(2):
+                fn()
+        torch.cuda.current_stream().wait_stream(s)
+        torch.cuda.synchronize()
+        self.g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.g):
+            fn()
+        torch.cuda.synchronize()
+
+    def __call__(self):
+        self.g.replay()
+
+
+def bench_moe(ckl, dev, timer, peak):
+    """W4A16 (asym int4 g128) SwiGLU MoE layer, E=64, top-6, d=2048,
+    F=1408, T in {1,4,16,64}; weights N(0,0.02), X and logits N(0,1); cold L2."""
+    import torch
+    E, k, d, F = 64, 6, 2048, 1408
+    g = torch.Generator(device=dev)
+    g.manual_seed(44)
+    mk = lambda *sh: (torch.randn(*sh, generator=g, device=dev) * 0.02).half()
+    q = [ckl.QuantWeights(4, mk(E, d, F), group=128, asym=True) for _ in range(2)]
+    q.append(ckl.QuantWeights(4, mk(E, F, d), group=128, asym=True))
+    layer = ckl.MoeLayer(*q)
+    res = {}
+    for T in (1, 4, 16, 64):
+        lg = torch.randn((T, E), generator=g, device=dev)
+        X = torch.randn((T, d), generator=g, device=dev).half()
+        out = torch.empty((T, d), dtype=torch.float16, device=dev)
+        ids = torch.empty((T, k), dtype=torch.int32, device=dev)
+        wts = torch.empty((T, k), dtype=torch.float32, device=dev)
+        ws = torch.empty(layer.workspace_size(T, k), dtype=torch.uint8, device=dev)
+        fn = lambda: layer.forward(lg, X, k, out=out, ids=ids, wts=wts, workspace=ws)
+        t_eager = timer(fn)
+        graph = GraphStep(fn, dev)
+        t_graph = timer(graph)
+        byts = _moe_active_bytes(q, ids.cpu().numpy()) + T * d * 2 * 2
+        res[f"T={T}"] = {"us_eager": round(t_eager * 1e3, 2), "us_graph": round(t_graph * 1e3, 2),
+                         "active_experts": int(len(set(ids.cpu().numpy().ravel().tolist()))),
+                         "bytes": byts, "GB/s_graph": round(byts / (t_graph * 1e-3) / 1e9, 1),
+                         "frac_of_measured_hbm": round(byts / (t_graph * 1e-3) / 1e9 / peak, 3),
+                         "launches": 4 + sum(1 for w in (q[0], q[2])
+                                             if w.workspace_size(T * k, w is q[0]) > 0)}
+        del graph
+    del q, layer
+    torch.cuda.empty_cache()
+    return res
+
+
+def bench_mixtral_layer(ckl, dev, timer, peak):
+    """paged GQA attention (B=32, L=4096, Hq=32, Hkv=8) followed by the
+    MoE block (E=8, top-2, d=4096, F=14336, SwiGLU, int8 per output channel), T=32 tokens;
+    one step = attention + MoE, replayed from one CUDA graph; cold L2."""
+    import torch
+    B, L = 32, 4096
+    E, k, d, F = 8, 2, 4096, 14336
+    d_attn, _ = paged_batch([L] * B, dev, seed=55)
+    nc, ct = ckl.plan_chunks(HQ // HKV, B, HKV, L)
+    pa = ckl.make_params(**d_attn, num_chunks=nc, chunk_tokens=ct)
+    a_out = torch.empty_like(d_attn["q"])
+    a_lse = torch.empty((B, HQ), dtype=torch.float32, device=dev)
+    a_ws = torch.empty(max(ckl.workspace_size(pa), 256), dtype=torch.uint8, device=dev)
+    g = torch.Generator(device=dev)
+    g.manual_seed(55)
+    mk = lambda *sh: (torch.randn(*sh, generator=g, device=dev) * 0.02).half()
+    q = [ckl.QuantWeights(8, mk(E, d, F), group=d), ckl.QuantWeights(8, mk(E, d, F), group=d),
+         ckl.QuantWeights(8, mk(E, F, d), group=F)]
+    layer = ckl.MoeLayer(*q)
+    lg = torch.randn((B, E), generator=g, device=dev)
+    X = torch.randn((B, d), generator=g, device=dev).half()
+    out = torch.empty((B, d), dtype=torch.float16, device=dev)
+    ids = torch.empty((B, k), dtype=torch.int32, device=dev)
+    ws = torch.empty(layer.workspace_size(B, k), dtype=torch.uint8, device=dev)
+
+    def attn():
+        ckl.decode_attention(**d_attn, num_chunks=nc, chunk_tokens=ct, out=a_out, lse=a_lse,
+                             workspace=a_ws)
+
+    def moe():
+        layer.forward(lg, X, k, out=out, ids=ids, workspace=ws)
+
+    def step():
+        attn()
+        moe()
+
+    t_attn = timer(GraphStep(attn, dev))
+    t_moe = timer(GraphStep(moe, dev))
+    t_step = timer(GraphStep(step, dev))
+    attn_bytes = algorithmic_bytes([L] * B)
+    moe_bytes = _moe_active_bytes(q, ids.cpu().numpy()) + B * d * 2 * 2
+    res = {"us_step": round(t_step * 1e3, 2), "us_attention": round(t_attn * 1e3, 2),
+           "us_moe": round(t_moe * 1e3, 2), "attention_bytes": attn_bytes, "moe_bytes": moe_bytes,
+           "GB/s_step": round((attn_bytes + moe_bytes) / (t_step * 1e-3) / 1e9, 1),
+           "frac_of_measured_hbm": round((attn_bytes + moe_bytes) / (t_step * 1e-3) / 1e9 / peak, 3),
+           "moe_active_experts": int(len(set(ids.cpu().numpy().ravel().tolist())))}
+    del q, layer, d_attn
+    torch.cuda.empty_cache()
+    return res
+
+
 # ------------------------------------------------------------------ our arm
 def run_ours(args):
     import numpy as np
@@ -533,6 +650,8 @@ def run_ours(args):
         timer = ColdTimer(dev)
         extras["config2_sweep"] = sweep_config2(ckl, dev, timer, peak)
         extras["config3_cascade"] = bench_cascade(ckl, dev, timer, peak)
+        extras["config4_moe_w4a16_layer"] = bench_moe(ckl, dev, timer, peak)
+        extras["config5_mixtral_layer"] = bench_mixtral_layer(ckl, dev, timer, peak)
         extras["extras_timing"] = "cold L2 (256 MB memset before each sample), median of 15"
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

@@ -49,6 +49,13 @@ class CascadePlan(C.Structure):
                 ("suffix", DecodeParams)]
 
 
+class MoeWeights(C.Structure):
+    """ckl_moe_weights (the packed buffers of QuantWeights, 03_moe_wq_decode.cu:281-333)."""
+    _fields_ = [("bits", C.c_int), ("E", C.c_int), ("K", C.c_int), ("N", C.c_int),
+                ("group", C.c_int), ("asym", C.c_int), ("packed", C.c_void_p),
+                ("scales", C.c_void_p), ("zeros", C.c_void_p)]
+
+
 _lib = None
 
 # name -> (restype, argtypes); every function declared in include/ckl.h
@@ -78,6 +85,32 @@ _SIGS = {
                                      C.c_void_p]),
     "ckl_cascade_decode": (C.c_int, [C.POINTER(CascadePlan), C.c_void_p, C.c_void_p,
                                      C.c_void_p, C.c_size_t, C.c_void_p]),
+    "ckl_moe_packed_bytes": (C.c_size_t, [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int]),
+    "ckl_moe_scale_count": (C.c_size_t, [C.c_int, C.c_int, C.c_int, C.c_int]),
+    "ckl_moe_zero_words": (C.c_size_t, [C.c_int, C.c_int, C.c_int, C.c_int]),
+    "ckl_moe_pack_weights": (C.c_int, [C.c_void_p, C.POINTER(MoeWeights), C.c_void_p]),
+    "ckl_moe_dequant_weights": (C.c_int, [C.POINTER(MoeWeights), C.c_void_p, C.c_void_p]),
+    "ckl_moe_gemm_workspace_size": (C.c_size_t, [C.POINTER(MoeWeights), C.c_int, C.c_int,
+                                                 C.c_int]),
+    "ckl_moe_expert_gemm": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int,
+                                      C.POINTER(MoeWeights), C.c_int, C.c_void_p, C.c_size_t,
+                                      C.c_void_p]),
+    "ckl_moe_expert_gemm_ex": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int,
+                                         C.POINTER(MoeWeights), C.POINTER(MoeWeights),
+                                         C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_size_t,
+                                         C.c_void_p]),
+    "ckl_moe_route_permute": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int,
+                                        C.c_int, C.c_void_p, C.c_void_p, C.c_void_p,
+                                        C.c_void_p, C.c_void_p, C.c_void_p, C.c_int,
+                                        C.c_void_p, C.c_void_p]),
+    "ckl_moe_combine": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p,
+                                  C.c_int, C.c_int, C.c_int, C.c_void_p]),
+    "ckl_moe_layer_workspace_size": (C.c_size_t, [C.c_int, C.c_int, C.POINTER(MoeWeights),
+                                                  C.POINTER(MoeWeights)]),
+    "ckl_moe_layer": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_int,
+                                C.POINTER(MoeWeights), C.POINTER(MoeWeights),
+                                C.POINTER(MoeWeights), C.c_void_p, C.c_void_p, C.c_void_p,
+                                C.c_void_p, C.c_size_t, C.c_void_p]),
 }
 
 
@@ -300,3 +333,133 @@ def cascade_decode(cp: CascadePlan, out=None, lse=None, workspace=None, stream=N
     check(lib().ckl_cascade_decode(C.byref(cp), _ptr(out), _ptr(lse), _ptr(workspace), ws_bytes,
                                    _stream(stream)), "ckl_cascade_decode")
     return out, lse
+
+
+# ------------------------------------------------------------------ MoE
+class QuantWeights:
+    """QuantWeights (03_moe_wq_decode.cu:281-333): packs fp16 W [E][K][N] (a CUDA tensor)
+    into the library's format. bits 4 (group 128; asym=True adds zero points), 8 (group 128
+    or group=K per output channel) or 16."""
+
+    def __init__(self, bits, W, group=128, asym=False, stream=None):
+        torch = _torch()
+        _need(W, torch.float16, "W")
+        E, K, N = W.shape
+        dev = W.device
+        if bits == 16:
+            group = K
+        self.bits, self.E, self.K, self.N, self.group, self.asym = bits, E, K, N, group, asym
+        L = lib()
+        self.packed = torch.empty(L.ckl_moe_packed_bytes(bits, E, K, N, group), dtype=torch.uint8,
+                                  device=dev)
+        ns = L.ckl_moe_scale_count(E, K, N, group) if bits != 16 else 1
+        self.scales = torch.empty(max(ns, 1), dtype=torch.float16, device=dev)
+        nz = L.ckl_moe_zero_words(E, K, N, group) if asym else 1
+        self.zeros = torch.zeros(max(nz, 1), dtype=torch.int32, device=dev)
+        self.w = MoeWeights(bits, E, K, N, group, int(asym), self.packed.data_ptr(),
+                            self.scales.data_ptr() if bits != 16 else None,
+                            self.zeros.data_ptr() if asym else None)
+        check(L.ckl_moe_pack_weights(_ptr(W), C.byref(self.w), _stream(stream)),
+              "ckl_moe_pack_weights")
+
+    def dequant(self, stream=None):
+        torch = _torch()
+        out = torch.empty((self.E, self.K, self.N), dtype=torch.float32, device=self.packed.device)
+        check(lib().ckl_moe_dequant_weights(C.byref(self.w), _ptr(out), _stream(stream)),
+              "ckl_moe_dequant_weights")
+        return out
+
+    def bytes_per_expert(self):
+        """Algorithmic bytes of one expert: codes + scales (+ zero points)."""
+        b = self.K * self.N * self.bits // 8
+        if self.bits != 16:
+            b += (self.K // self.group) * self.N * 2
+        if self.asym:
+            b += (self.K // self.group) * self.N // 2
+        return b
+
+    def workspace_size(self, A, swiglu=False, force_ksplit=0):
+        return lib().ckl_moe_gemm_workspace_size(C.byref(self.w), A, int(swiglu), force_ksplit)
+
+    def run(self, Xp, Yp, offsets, A, force_ksplit=0, workspace=None, stream=None):
+        """QuantWeights::run: Yp[r] = Xp[r] . W_e for the rows of each expert."""
+        torch = _torch()
+        need = self.workspace_size(A, False, force_ksplit)
+        if need and (workspace is None or workspace.numel() * workspace.element_size() < need):
+            workspace = torch.empty(need, dtype=torch.uint8, device=Xp.device)
+        wsb = 0 if workspace is None else workspace.numel() * workspace.element_size()
+        check(lib().ckl_moe_expert_gemm(_ptr(Xp), _ptr(Yp), _ptr(offsets), A, C.byref(self.w),
+                                        force_ksplit, _ptr(workspace), wsb, _stream(stream)),
+              "ckl_moe_expert_gemm")
+
+
+def expert_gemm_ex(X, row_src, offsets, A, gate, up=None, y_f32=False, force_ksplit=0,
+                   stream=None):
+    torch = _torch()
+    N = gate.N
+    Y = torch.empty((A, N), dtype=torch.float32 if y_f32 else torch.float16, device=X.device)
+    need = gate.workspace_size(A, up is not None, force_ksplit)
+    ws = torch.empty(max(need, 1), dtype=torch.uint8, device=X.device)
+    check(lib().ckl_moe_expert_gemm_ex(_ptr(X), _ptr(row_src), _ptr(offsets), A, C.byref(gate.w),
+                                       None if up is None else C.byref(up.w), _ptr(Y), int(y_f32),
+                                       force_ksplit, _ptr(ws), need, _stream(stream)),
+          "ckl_moe_expert_gemm_ex")
+    return Y
+
+
+def route_and_permute(logits, X, k, bm=0, permute=True, stream=None):
+    """MoeDecode::route_and_permute (03_moe_wq_decode.cu:382-389) -> dict of device tensors
+    ids, wts, counts, offsets, inv_perm, Xp (None unless permute), tiles (None unless bm)."""
+    torch = _torch()
+    T, E = logits.shape
+    dev = logits.device
+    d = X.shape[1] if X is not None else 0
+    i32 = dict(dtype=torch.int32, device=dev)
+    r = dict(ids=torch.empty((T, k), **i32), wts=torch.empty((T, k), dtype=torch.float32, device=dev),
+             counts=torch.empty(E, **i32), offsets=torch.empty(E + 1, **i32),
+             inv_perm=torch.empty(T * k, **i32), Xp=None, tiles=None)
+    if permute:
+        r["Xp"] = torch.empty((T * k, d), dtype=torch.float16, device=dev)
+    if bm:
+        r["tiles"] = torch.empty(E + 1, **i32)
+    check(lib().ckl_moe_route_permute(_ptr(logits), _ptr(X), T, E, k, d, _ptr(r["ids"]),
+                                      _ptr(r["wts"]), _ptr(r["counts"]), _ptr(r["offsets"]),
+                                      _ptr(r["inv_perm"]), _ptr(r["Xp"]), bm, _ptr(r["tiles"]),
+                                      _stream(stream)), "ckl_moe_route_permute")
+    return r
+
+
+def combine(Yp, inv_perm, wts, T, k, stream=None):
+    """moe_combine (common/moe.cuh:97-119) -> out fp16 [T][f]."""
+    torch = _torch()
+    f = Yp.shape[1]
+    out = torch.empty((T, f), dtype=torch.float16, device=Yp.device)
+    check(lib().ckl_moe_combine(_ptr(Yp), int(Yp.dtype == torch.float32), _ptr(inv_perm),
+                                _ptr(wts), _ptr(out), T, k, f, _stream(stream)), "ckl_moe_combine")
+    return out
+
+
+class MoeLayer:
+    """The SwiGLU MoE decode layer over packed gate/up [E][d][F] and down [E][F][d]."""
+
+    def __init__(self, gate: QuantWeights, up: QuantWeights, down: QuantWeights):
+        self.gate, self.up, self.down = gate, up, down
+
+    def workspace_size(self, T, k):
+        return lib().ckl_moe_layer_workspace_size(T, k, C.byref(self.gate.w), C.byref(self.down.w))
+
+    def forward(self, logits, X, k, out=None, ids=None, wts=None, workspace=None, stream=None):
+        torch = _torch()
+        T = X.shape[0]
+        dev = X.device
+        if out is None:
+            out = torch.empty((T, self.down.N), dtype=torch.float16, device=dev)
+        need = self.workspace_size(T, k)
+        if workspace is None or workspace.numel() * workspace.element_size() < need:
+            workspace = torch.empty(need, dtype=torch.uint8, device=dev)
+        check(lib().ckl_moe_layer(_ptr(logits), _ptr(X), T, k, C.byref(self.gate.w),
+                                  C.byref(self.up.w), C.byref(self.down.w), _ptr(out), _ptr(ids),
+                                  _ptr(wts), _ptr(workspace),
+                                  workspace.numel() * workspace.element_size(), _stream(stream)),
+              "ckl_moe_layer")
+        return out

@@ -193,6 +193,103 @@ CKL_API ckl_status ckl_cascade_decode(const ckl_cascade_plan_t* plan, void* out,
                                       void* workspace, size_t workspace_bytes, void* stream);
 
 /* ======================================================================================
+ * Weight-only quantised MoE decode layer (W4A16 / W8A16 / fp16 experts)
+ * ==================================================================================== */
+
+/* Packed expert weights (QuantWeights, 03_moe_wq_decode.cu:281-333). A weight matrix is
+ * W[e][k][n], e < E experts, k < K (the reduction dim, the reference's d) and n < N (the
+ * output dim, the reference's f), fp16 row-major like the reference's [E][d][f].
+ *   packed  device, ckl_moe_packed_bytes(bits, E, K, N, group) bytes: 16-column strips of
+ *           per-group records holding each lane's mma.sync A fragments and the group's
+ *           scales/zeros (layout documented in csrc/moe_common.cuh)
+ *   scales  device fp16 [E][K/group][N] (the reference's Sc layout, 03:71); unused at 16 bits
+ *   zeros   device uint32 [E][K/group][N/8], 4-bit zero point of column n in nibble n%8
+ *           (asymmetric int4 only; symmetric codes are offset-binary, zero 8 or 128)
+ * bits 4: group 128 (symmetric as the reference, or asym = 1 with zero points);
+ * bits 8: symmetric, group 128 (the reference) or group = K (per output channel);
+ * bits 16: fp16 weights (group ignored). Requires E <= 256, K % 128 == 0, N % 8 == 0. */
+typedef struct ckl_moe_weights {
+    int bits;
+    int E, K, N;
+    int group;
+    int asym;
+    void* packed;
+    void* scales;
+    void* zeros;
+} ckl_moe_weights;
+
+/* Sizes of the three buffers of ckl_moe_weights (bytes; fp16 elements; uint32 words). */
+CKL_API size_t ckl_moe_packed_bytes(int bits, int E, int K, int N, int group);
+CKL_API size_t ckl_moe_scale_count(int E, int K, int N, int group);
+CKL_API size_t ckl_moe_zero_words(int E, int K, int N, int group);
+
+/* pack_weights<BITS> (03_moe_wq_decode.cu:48-87): quantises fp16 W [E][K][N] (device) into
+ * the caller-allocated buffers of *w. Symmetric: s = fp16(max|w| / qmax), q = clamp(rn(w/s))
+ * with the rounded scale (03:70-81). Asymmetric int4 (north-star extension):
+ * s = fp16((max(w,0) - min(w,0)) / 15), z = clamp(rn(-min(w,0)/s), 0, 15),
+ * q = clamp(rn(w/s) + z, 0, 15). */
+CKL_API ckl_status ckl_moe_pack_weights(const void* W, ckl_moe_weights* w, void* stream);
+
+/* The dequantised weights the GEMM uses, fp32 [E][K][N]: (q - z) * s exactly
+ * (host_weight, 03_moe_wq_decode.cu:336-348). */
+CKL_API ckl_status ckl_moe_dequant_weights(const ckl_moe_weights* w, float* W_out, void* stream);
+
+/* Workspace of ckl_moe_expert_gemm(_ex) for A permuted rows (split-K partials; 0 when the
+ * launch does not split K). swiglu = 1 for a gate/up pair. */
+CKL_API size_t ckl_moe_gemm_workspace_size(const ckl_moe_weights* w, int A, int swiglu,
+                                           int force_ksplit);
+
+/* QuantWeights::run (03_moe_wq_decode.cu:318-332): Yp[r] = Xp[r] . dequant(W_e) for every
+ * expert e and row r in [offsets[e], offsets[e+1]); Xp fp16 [A][K], Yp fp16 [A][N]. The
+ * grid is an upper bound of min(E, A) expert slots resolved on the device from offsets:
+ * no host sync. force_ksplit > 0 overrides the K split (pick_ksplit 03:306-315). */
+CKL_API ckl_status ckl_moe_expert_gemm(const void* Xp, void* Yp, const int* offsets, int A,
+                                       const ckl_moe_weights* w, int force_ksplit,
+                                       void* workspace, size_t workspace_bytes, void* stream);
+
+/* Extended form: rows gathered from X through row_src[A] (NULL: X is already permuted);
+ * with `up` != NULL the gate/up pair is fused: Y = fp16(silu(X.Wg) * (X.Wu)) (the SwiGLU
+ * intermediate, north-star extension); y_f32 = 1 writes fp32 Y. */
+CKL_API ckl_status ckl_moe_expert_gemm_ex(const void* X, const int* row_src, const int* offsets,
+                                          int A, const ckl_moe_weights* gate,
+                                          const ckl_moe_weights* up, void* Y, int y_f32,
+                                          int force_ksplit, void* workspace,
+                                          size_t workspace_bytes, void* stream);
+
+/* MoeDecode::route_and_permute (03_moe_wq_decode.cu:382-389): router_topk (common/moe.cuh:
+ * 23-72: softmax top-k, ties to the lower id, weights renormalised over the chosen k),
+ * counts (moe_count), offsets[E+1] (moe_scan_offsets), optional tile offsets
+ * tiles[E+1] = exclusive scan of ceil(count/bm) (moe_scan, 02_moe_grouped_gemm.cu:71-82),
+ * inv_perm[T*k], and when Xp != NULL the permuted rows Xp[inv_perm[i]] = X[i/k]. The slot
+ * order is the stable rank by (expert, token, slot) -- deterministic, unlike the
+ * reference's atomicAdd. logits fp32 [T][E]; E <= 256, k <= 8, T*k <= 4096. */
+CKL_API ckl_status ckl_moe_route_permute(const float* logits, const void* X, int T, int E, int k,
+                                         int d, int* ids, float* wts, int* counts, int* offsets,
+                                         int* inv_perm, void* Xp, int bm, int* tiles,
+                                         void* stream);
+
+/* moe_combine (common/moe.cuh:97-119): out[t] = sum_{j<k} wts[t][j] * Yp[inv_perm[t*k+j]]
+ * accumulated in fp32 in fixed j order, written fp16 [T][f]. Yp fp16 (y_f32 = 0) or fp32. */
+CKL_API ckl_status ckl_moe_combine(const void* Yp, int y_f32, const int* inv_perm,
+                                   const float* wts, void* out, int T, int k, int f,
+                                   void* stream);
+
+/* Workspace of ckl_moe_layer. */
+CKL_API size_t ckl_moe_layer_workspace_size(int T, int k, const ckl_moe_weights* gate,
+                                            const ckl_moe_weights* down);
+
+/* The MoE decode layer (MoeDecode route_and_permute + expert GEMM + combine,
+ * 03_moe_wq_decode.cu:350-391, with a SwiGLU expert per the north star): routing, fused
+ * gate/up GEMM with h = fp16(silu(x Wg) * (x Wu)), down GEMM, fixed-order combine.
+ * gate/up are [E][d][F], down is [E][F][d]; X fp16 [T][d]; out fp16 [T][d]. ids_out /
+ * wts_out (optional, [T][k]) receive the routing. No host sync. */
+CKL_API ckl_status ckl_moe_layer(const float* logits, const void* X, int T, int k,
+                                 const ckl_moe_weights* gate, const ckl_moe_weights* up,
+                                 const ckl_moe_weights* down, void* out, int* ids_out,
+                                 float* wts_out, void* workspace, size_t workspace_bytes,
+                                 void* stream);
+
+/* ======================================================================================
  * Measurement
  * ==================================================================================== */
 

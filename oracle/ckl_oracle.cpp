@@ -303,6 +303,23 @@ void ora_normal(size_t n, unsigned seed, float mean, float stddev, uint16_t* out
     }
 }
 
+// init_uniform (common/moe.cuh:131-138): the reference's hash-based device generator of
+// U(-scale, scale) fp16 values, element i from a 32-bit integer hash of (i, seed). Restated
+// on the host so the MoE tests use exactly the reference test's X and W.
+void ora_init_uniform(uint16_t* p, size_t n, uint32_t seed, float scale) {
+    for (size_t i = 0; i < n; i++) {
+        uint32_t x = (uint32_t)(i ^ (i >> 32)) * 2654435761u;
+        x ^= seed;
+        x ^= x >> 16;
+        x *= 0x7feb352du;
+        x ^= x >> 15;
+        x *= 0x846ca68bu;
+        x ^= x >> 16;
+        const float u = (float)(x >> 8) * (1.0f / 16777216.0f);
+        p[i] = f2h((2.f * u - 1.f) * scale);
+    }
+}
+
 // ---------------------------------------------------------------- MoE routing
 // Routing of the fp64 MoE reference (02_moe_grouped_gemm.cu:273-290): p = softmax(logits)
 // in fp64, k rounds of argmax with ties to the lower expert id, weights p_i / sum of the

@@ -49,6 +49,7 @@ def lib():
             "ora_shared_prefix_pages": (i, [vp, vp, i]),
             "ora_make_logits": (None, [i, i, u, i, i, vp]),
             "ora_normal": (None, [sz, u, f, f, vp, vp]),
+            "ora_init_uniform": (None, [vp, sz, u, f]),
             "ora_route": (None, [vp, i, i, i, vp, vp]),
             "ora_permute": (None, [vp, i, i, i, vp, vp, vp, vp]),
             "ora_quant_sym": (None, [vp, i, i, i, i, i, vp, vp, i]),
@@ -163,6 +164,13 @@ def normal(shape, seed, mean=0.0, std=1.0, fp16=True):
     else:
         a = np.empty(shape, np.float32)
         lib().ora_normal(n, seed, mean, std, None, _p(a))
+    return a
+
+
+def init_uniform(shape, seed, scale):
+    """The reference's init_uniform hash generator (common/moe.cuh:131-138), fp16."""
+    a = np.empty(shape, np.float16)
+    lib().ora_init_uniform(_p(a), a.size, seed, scale)
     return a
 
 
