@@ -40,6 +40,25 @@ ckl_status encode_tiled(CUtensorMap* map, CUtensorMapDataType dtype, int rank, v
                         const uint64_t* dims, const uint64_t* strides_bytes,
                         const uint32_t* box, CUtensorMapSwizzle swizzle);
 
+// Launches `fn` on `stream`; with pdl = true the launch may begin while the previous kernel
+// on the stream is still running (programmatic dependent launch): the kernel must call
+// pdl_wait() before it reads anything that kernel writes.
+inline cudaError_t launch(const void* fn, dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                          void** args, bool pdl) {
+    if (!pdl) return cudaLaunchKernel(fn, grid, block, args, smem, stream);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelExC(&cfg, fn, args);
+}
+
 inline int ceil_div(int a, int b) { return (a + b - 1) / b; }
 inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 

@@ -75,6 +75,10 @@ struct GemmArgs {
     unsigned* err;
     unsigned long long timeout_ns;
     int E, K, N, ksplit, A, y_f32;
+    // 0: normal launch. 1: launched dependent on the previous kernel, which produced the
+    // offsets: wait before anything. 2: dependent on a kernel that produced only X (the
+    // offsets are older): prefetch the first weight stages, then wait before the X rows.
+    int dep;
 };
 
 // The j-th expert (in id order) that has rows, or -1. Every lane returns the same value.
@@ -108,7 +112,8 @@ struct Cfg {
     static constexpr int SBYTES = (WBYTES + XROWS * XSTRIDE + 127) / 128 * 128;
     static constexpr int STAGES_RAW = RING_BYTES / SBYTES;
     static constexpr int STAGES = STAGES_RAW > MAX_STAGES ? MAX_STAGES : STAGES_RAW;
-    static constexpr int RED = TILES * 32 * TMAX * 4 * MATS * 4;   // cross-warp reduction
+    static constexpr int RVALS = TMAX * 4 * MATS;                  // fp32 values per lane
+    static constexpr int RED = TILES * 32 * RVALS * 4;              // cross-warp reduction
     static constexpr int SMEM = 128 + STAGES * SBYTES + RED + 2 * MAX_STAGES * 8;
 };
 
@@ -223,8 +228,12 @@ moe_gemm_kernel(const GemmArgs a) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int quad = blockIdx.x;
 
+    if (a.dep == 1) pdl_wait();                          // offsets come from the previous kernel
     const int e = nth_active_expert(a.offsets, a.E, blockIdx.y);
-    if (e < 0) return;                                   // surplus slot of the upper bound
+    if (e < 0) {                                         // surplus slot of the upper bound
+        pdl_trigger();
+        return;
+    }
     const int row_beg = __ldg(a.offsets + e), n_e = __ldg(a.offsets + e + 1) - row_beg;
     const int ngroups = a.K / KGROUP_STAGE;
     const int per = (ngroups + a.ksplit - 1) / a.ksplit;
@@ -241,6 +250,7 @@ moe_gemm_kernel(const GemmArgs a) {
     }
     __syncthreads();
     const uint64_t deadline = globaltimer() + a.timeout_ns;
+    if (a.dep != 2) pdl_trigger();
 
     if (warp == CONSUMERS) {
         // ---------------------------------------------------------------- producer warp
@@ -249,6 +259,23 @@ moe_gemm_kernel(const GemmArgs a) {
         const int lgroup = C::EMBED ? KGROUP_STAGE : a.K;
         const uint8_t* w0 = a.W0 + block_offset(BITS, lgroup, a.K, a.N, e, quad, 0);
         const uint8_t* w1 = SWIGLU ? a.W1 + block_offset(BITS, lgroup, a.K, a.N, e, quad, 0) : nullptr;
+        // dep 2: the weights of the first stages do not depend on the previous kernel --
+        // start streaming them, then wait for it before any token row is read
+        int npre = 0;
+        if (a.dep == 2) {
+            npre = min(C::STAGES, nst);
+            if (lane == 0)
+                for (int si = 0; si < npre; si++) {
+                    const int grp = g_beg + si * GPS, ngs = min(GPS, g_end - grp);
+                    uint8_t* st = ring + (size_t)si * C::SBYTES;
+                    mbar_expect_tx(&full[si], C::MATS * ngs * C::GBLK);
+                    bulk_load(st, w0 + (size_t)grp * C::GBLK, ngs * C::GBLK, &full[si], wpol);
+                    if (SWIGLU)
+                        bulk_load(st + GPS * C::GBLK, w1 + (size_t)grp * C::GBLK, ngs * C::GBLK, &full[si], wpol);
+                }
+            pdl_wait();
+            pdl_trigger();
+        }
         int ok = 1, seq = 0;
         for (int p = 0; p < npass && ok; p++) {
             const int r0 = p * C::XROWS, nr = min(C::XROWS, n_e - r0);
@@ -265,10 +292,14 @@ moe_gemm_kernel(const GemmArgs a) {
                 const int grp = g_beg + si * GPS;
                 const int ngs = min(GPS, g_end - grp);
                 if (lane == 0) {
-                    mbar_arrive_expect_tx(&full[s], C::MATS * ngs * C::GBLK + nr * ngs * 256);
-                    bulk_load(st, w0 + (size_t)grp * C::GBLK, ngs * C::GBLK, &full[s], wpol);
-                    if (SWIGLU)
-                        bulk_load(st + GPS * C::GBLK, w1 + (size_t)grp * C::GBLK, ngs * C::GBLK, &full[s], wpol);
+                    if (seq < npre) {                      // weights already in flight
+                        mbar_arrive_expect_tx(&full[s], nr * ngs * 256);
+                    } else {
+                        mbar_arrive_expect_tx(&full[s], C::MATS * ngs * C::GBLK + nr * ngs * 256);
+                        bulk_load(st, w0 + (size_t)grp * C::GBLK, ngs * C::GBLK, &full[s], wpol);
+                        if (SWIGLU)
+                            bulk_load(st + GPS * C::GBLK, w1 + (size_t)grp * C::GBLK, ngs * C::GBLK, &full[s], wpol);
+                    }
                 }
                 __syncwarp();
                 if (lane < nr)
@@ -288,6 +319,7 @@ moe_gemm_kernel(const GemmArgs a) {
     }
 
     // -------------------------------------------------------------------- consumer warps
+    if (a.dep == 2) pdl_trigger();
     const int g = lane >> 2, t = lane & 3;
     const int tile = warp % TILES, half = warp / TILES;
     const int col_lo = quad * 64 + tile * 16 + g, col_hi = col_lo + 8;
@@ -316,14 +348,16 @@ moe_gemm_kernel(const GemmArgs a) {
         if (!__all_sync(0xffffffffu, ok)) return;          // timed out (already recorded)
 
         // the two warps of a tile hold partial sums over alternate groups: add them
-        float* rw = red + ((size_t)tile * 32 + lane) * (TMAX * 4 * C::MATS);
+        // [value][tile][lane]: consecutive lanes hit consecutive banks
+        float* rw = red + tile * 32 + lane;
+        constexpr int RS = TILES * 32;
         if (half == 1) {
 #pragma unroll
             for (int i = 0; i < TMAX; i++)
 #pragma unroll
                 for (int c = 0; c < 4; c++) {
-                    rw[i * 4 + c] = acc0[i][c];
-                    if (SWIGLU) rw[TMAX * 4 + i * 4 + c] = acc1[i][c];
+                    rw[(i * 4 + c) * RS] = acc0[i][c];
+                    if (SWIGLU) rw[(TMAX * 4 + i * 4 + c) * RS] = acc1[i][c];
                 }
         }
         consumer_bar();
@@ -337,8 +371,8 @@ moe_gemm_kernel(const GemmArgs a) {
                     const int r = 8 * i + 2 * t + (c & 1);
                     const int col = (c & 2) ? col_hi : col_lo;
                     if (r >= nr || col >= a.N) continue;
-                    float v0 = (acc0[i][c] + rw[i * 4 + c]) * ((c & 2) ? pc0_hi : pc0_lo);
-                    float v1 = SWIGLU ? (acc1[i][c] + rw[TMAX * 4 + i * 4 + c]) * ((c & 2) ? pc1_hi : pc1_lo) : 0.f;
+                    float v0 = (acc0[i][c] + rw[(i * 4 + c) * RS]) * ((c & 2) ? pc0_hi : pc0_lo);
+                    float v1 = SWIGLU ? (acc1[i][c] + rw[(TMAX * 4 + i * 4 + c) * RS]) * ((c & 2) ? pc1_hi : pc1_lo) : 0.f;
                     const size_t o = (size_t)(row0 + r) * a.N + col;
                     if (a.ksplit > 1) {
                         float* P = static_cast<float*>(a.Y) + (size_t)blockIdx.z * a.A * a.N * C::MATS;
@@ -364,6 +398,8 @@ moe_gemm_kernel(const GemmArgs a) {
 template <bool SWIGLU>
 __global__ void splitk_reduce_kernel(const float* __restrict__ P, void* Y, int y_f32, size_t n,
                                      int ksplit) {
+    pdl_wait();
+    pdl_trigger();
     const size_t stride = SWIGLU ? 2 * n : n;
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
          i += (size_t)gridDim.x * blockDim.x) {
@@ -617,7 +653,8 @@ namespace ckl {
 namespace moe {
 ckl_status expert_gemm(const void* X, const int* row_src, const int* offsets, int A, int max_rows,
                        const ckl_moe_weights* w0, const ckl_moe_weights* w1, void* Y, int y_f32,
-                       int force_ksplit, void* workspace, size_t workspace_bytes, void* stream);
+                       int force_ksplit, void* workspace, size_t workspace_bytes, void* stream,
+                       int dep = 0);
 }  // namespace moe
 }  // namespace ckl
 
@@ -700,7 +737,8 @@ namespace moe {
 // token reaches an expert at most once); it sizes the token tiles of a pass.
 ckl_status expert_gemm(const void* X, const int* row_src, const int* offsets, int A, int max_rows,
                        const ckl_moe_weights* w0, const ckl_moe_weights* w1, void* Y, int y_f32,
-                       int force_ksplit, void* workspace, size_t workspace_bytes, void* stream) {
+                       int force_ksplit, void* workspace, size_t workspace_bytes, void* stream,
+                       int dep) {
     ckl_status st = check_weights(w0, "moe_expert_gemm");
     if (st != CKL_OK) return st;
     const bool swiglu = w1 != nullptr;
@@ -746,20 +784,20 @@ ckl_status expert_gemm(const void* X, const int* row_src, const int* offsets, in
     a.ksplit = ks;
     a.A = A;
     a.y_f32 = y_f32;
+    a.dep = dep;
     void* args[] = {&a};
     const Variant v = gemm_variant(w0->bits, swiglu, grouped);
     dim3 grid((unsigned)quads, (unsigned)slots, (unsigned)ks);
     const cudaStream_t s = (cudaStream_t)stream;
-    CKL_CUDA_TRY(cudaLaunchKernel(v.fn, grid, dim3(GTHREADS), args, v.smem, s));
+    CKL_CUDA_TRY(launch(v.fn, grid, dim3(GTHREADS), v.smem, s, args, dep != 0));
     if (ks > 1) {
-        const size_t n = (size_t)A * w0->N;
-        if (swiglu)
-            splitk_reduce_kernel<true><<<256, 256, 0, s>>>(static_cast<const float*>(workspace), Y,
-                                                           y_f32, n, ks);
-        else
-            splitk_reduce_kernel<false><<<256, 256, 0, s>>>(static_cast<const float*>(workspace), Y,
-                                                            y_f32, n, ks);
-        CKL_CUDA_TRY(cudaGetLastError());
+        size_t n = (size_t)A * w0->N;
+        const float* P = static_cast<const float*>(workspace);
+        int ksv = ks;
+        void* rargs[] = {&P, &Y, &y_f32, &n, &ksv};
+        const void* rfn = swiglu ? reinterpret_cast<const void*>(splitk_reduce_kernel<true>)
+                                 : reinterpret_cast<const void*>(splitk_reduce_kernel<false>);
+        CKL_CUDA_TRY(launch(rfn, dim3(256), dim3(256), 0, s, rargs, dep != 0));
     }
     return CKL_OK;
 }

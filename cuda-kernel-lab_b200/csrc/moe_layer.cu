@@ -28,7 +28,8 @@ namespace moe {
 
 ckl_status expert_gemm(const void* X, const int* row_src, const int* offsets, int A, int max_rows,
                        const ckl_moe_weights* w0, const ckl_moe_weights* w1, void* Y, int y_f32,
-                       int force_ksplit, void* workspace, size_t workspace_bytes, void* stream);
+                       int force_ksplit, void* workspace, size_t workspace_bytes, void* stream,
+                       int dep);
 
 constexpr int MAX_E = 256;
 constexpr int MAX_K = 8;
@@ -56,6 +57,7 @@ route_kernel(const float* __restrict__ logits, int T, int E, int k, int* __restr
     float* s_lg = s_dyn;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int A = T * k;
+    pdl_trigger();                    // the expert GEMM may launch; it waits for our results
     for (int e = threadIdx.x; e < E; e += blockDim.x) s_cnt[e] = 0;
     const bool staged = T * (E + 1) <= ROUTE_SMEM_LOGITS;    // the launch sized s_lg for this
     const int lg_stride = E + 1;
@@ -160,6 +162,7 @@ __global__ void permute_rows_kernel(const __half* __restrict__ X, const int* __r
 template <bool F32>
 __global__ void combine_kernel(const void* __restrict__ Y, const int* __restrict__ inv_perm,
                                const float* __restrict__ wts, __half* __restrict__ out, int k, int f) {
+    pdl_wait();
     const int t = blockIdx.x;
     for (int c = threadIdx.x; c < f / 8; c += blockDim.x) {
         float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
@@ -335,11 +338,17 @@ ckl_status ckl_moe_layer(const float* logits, const void* X, int T, int k,
     route_kernel<<<1, ROUTE_THREADS, route_smem(T, E), s>>>(logits, T, E, k, ids, wts, counts,
                                                             offsets, inv_perm, row_src, 1, nullptr);
     CKL_CUDA_TRY(cudaGetLastError());
-    st = expert_gemm(X, row_src, offsets, A, T, gate, up, h, 0, 0, split, split_bytes, stream);
+    // gate/up waits for the routing; down prefetches its first weight stages while gate/up
+    // finishes (its offsets are the routing's, one kernel older); combine waits for down.
+    st = expert_gemm(X, row_src, offsets, A, T, gate, up, h, 0, 0, split, split_bytes, stream, 1);
     if (st != CKL_OK) return st;
-    st = expert_gemm(h, nullptr, offsets, A, T, down, nullptr, y, 1, 0, split, split_bytes, stream);
+    st = expert_gemm(h, nullptr, offsets, A, T, down, nullptr, y, 1, 0, split, split_bytes, stream,
+                     s2 > 0 ? 1 : 2);
     if (st != CKL_OK) return st;
-    return ckl_moe_combine(y, 1, inv_perm, wts, out, T, k, d, stream);
+    void* cargs[] = {&y, &inv_perm, &wts, &out, &k, const_cast<int*>(&d)};
+    CKL_CUDA_TRY(launch(reinterpret_cast<const void*>(combine_kernel<true>), dim3(T), dim3(256), 0,
+                        s, cargs, true));
+    return CKL_OK;
 }
 
 }  // extern "C"
