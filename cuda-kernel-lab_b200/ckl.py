@@ -56,6 +56,24 @@ class MoeWeights(C.Structure):
                 ("scales", C.c_void_p), ("zeros", C.c_void_p)]
 
 
+EP_MAX_RANKS = 8
+IPC_HANDLE_BYTES = 64
+
+
+class MoeEpComm(C.Structure):
+    """ckl_moe_ep_comm: rank, world, token capacity, top-k, experts, d_model and every
+    rank's communication window as mapped in this process."""
+    _fields_ = [("rank", C.c_int), ("world", C.c_int), ("T_cap", C.c_int), ("k", C.c_int),
+                ("E", C.c_int), ("d", C.c_int), ("windows", C.c_void_p * EP_MAX_RANKS)]
+
+
+class PeerGroup(C.Structure):
+    """ckl_peer_group: rank, world and every rank's flag window as mapped here."""
+    _fields_ = [("rank", C.c_int), ("world", C.c_int), ("windows", C.c_void_p * EP_MAX_RANKS)]
+
+
+PEER_WINDOW_BYTES = 256
+
 _lib = None
 
 # name -> (restype, argtypes); every function declared in include/ckl.h
@@ -111,6 +129,22 @@ _SIGS = {
                                 C.POINTER(MoeWeights), C.POINTER(MoeWeights),
                                 C.POINTER(MoeWeights), C.c_void_p, C.c_void_p, C.c_void_p,
                                 C.c_void_p, C.c_size_t, C.c_void_p]),
+    "ckl_decode_attention_gather": (C.c_int, [C.POINTER(DecodeParams), C.c_void_p, C.c_void_p,
+                                              C.c_int, C.c_int, C.c_void_p, C.c_size_t,
+                                              C.c_void_p]),
+    "ckl_gather_signal": (C.c_int, [C.POINTER(PeerGroup), C.c_int, C.c_void_p]),
+    "ckl_gather_wait": (C.c_int, [C.POINTER(PeerGroup), C.c_void_p]),
+    "ckl_moe_ep_window_bytes": (C.c_size_t, [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int]),
+    "ckl_ep_window_alloc": (C.c_int, [C.c_size_t, C.POINTER(C.c_void_p), C.c_void_p]),
+    "ckl_ep_window_open": (C.c_int, [C.c_void_p, C.POINTER(C.c_void_p)]),
+    "ckl_ep_window_close": (C.c_int, [C.c_void_p]),
+    "ckl_ep_window_free": (C.c_int, [C.c_void_p]),
+    "ckl_moe_ep_workspace_size": (C.c_size_t, [C.POINTER(MoeEpComm), C.POINTER(MoeWeights),
+                                               C.POINTER(MoeWeights)]),
+    "ckl_moe_ep_layer": (C.c_int, [C.POINTER(MoeEpComm), C.c_void_p, C.c_void_p, C.c_int,
+                                   C.POINTER(MoeWeights), C.POINTER(MoeWeights),
+                                   C.POINTER(MoeWeights), C.c_void_p, C.c_void_p, C.c_void_p,
+                                   C.c_void_p, C.c_size_t, C.c_void_p]),
 }
 
 
@@ -170,6 +204,20 @@ def _need(t, dtype, name):
     if t.dtype != dtype or not t.is_contiguous():
         raise CklError(1, name, f"expected contiguous {dtype}, got {t.dtype}")
     return t
+
+
+class _CudaArray:
+    def __init__(self, ptr, shape, typestr):
+        self.__cuda_array_interface__ = {"data": (int(ptr), False), "shape": tuple(shape),
+                                         "typestr": typestr, "strides": None, "version": 2}
+
+
+def device_view(ptr, shape, dtype):
+    """A torch tensor viewing raw device memory (a library-allocated window, own or
+    peer-mapped) without a copy; the memory must outlive the view."""
+    torch = _torch()
+    ts = {torch.float16: "<f2", torch.float32: "<f4", torch.int32: "<i4", torch.uint8: "|u1"}[dtype]
+    return torch.as_tensor(_CudaArray(ptr, shape, ts), device="cuda")
 
 
 # ------------------------------------------------------------------ decode attention
@@ -462,4 +510,159 @@ class MoeLayer:
                                   _ptr(wts), _ptr(workspace),
                                   workspace.numel() * workspace.element_size(), _stream(stream)),
               "ckl_moe_layer")
+        return out
+
+
+# ------------------------------------------------------------------ expert parallelism
+def ep_window_bytes(world, T_cap, k, E, d):
+    return lib().ckl_moe_ep_window_bytes(world, T_cap, k, E, d)
+
+
+class _LibWindows:
+    """CUDA IPC through the library: allocate + zero an own window, map / unmap peers."""
+
+    @staticmethod
+    def alloc(nbytes):
+        ptr, h = C.c_void_p(), (C.c_char * IPC_HANDLE_BYTES)()
+        check(lib().ckl_ep_window_alloc(nbytes, C.byref(ptr), h), "ckl_ep_window_alloc")
+        return ptr.value, bytes(h)
+
+    @staticmethod
+    def open(handle):
+        ptr = C.c_void_p()
+        check(lib().ckl_ep_window_open(C.c_char_p(handle), C.byref(ptr)), "ckl_ep_window_open")
+        return ptr.value
+
+    @staticmethod
+    def close(ptr):
+        check(lib().ckl_ep_window_close(C.c_void_p(ptr)), "ckl_ep_window_close")
+
+    @staticmethod
+    def free(ptr):
+        check(lib().ckl_ep_window_free(C.c_void_p(ptr)), "ckl_ep_window_free")
+
+
+def torch_exchange(group=None):
+    """exchange(handle) over a torch.distributed process group: every rank's bytes, in rank
+    order (all_gather_object; any backend)."""
+    import torch.distributed as dist
+
+    def exchange(blob):
+        out = [None] * dist.get_world_size(group)
+        dist.all_gather_object(out, blob, group=group)
+        return out
+    return exchange
+
+
+class IpcWindows:
+    """One device window per rank, allocated and zeroed here, every peer's mapped from its
+    IPC handle (windows in rank order in self.ptrs). `exchange(bytes) -> [bytes per rank]`
+    moves the handles (e.g. torch_exchange()); it is also the barrier that makes every
+    window zero before any rank uses one."""
+
+    def __init__(self, rank, world, nbytes, exchange, ipc=_LibWindows):
+        if not (1 <= world <= EP_MAX_RANKS and 0 <= rank < world):
+            raise CklError(1, "IpcWindows", f"rank {rank} of world {world} (<= {EP_MAX_RANKS})")
+        self.rank, self.world, self.nbytes = rank, world, nbytes
+        self._ipc, self._exchange = ipc, exchange
+        self.own, handle = ipc.alloc(nbytes)
+        handles = exchange(handle)
+        if len(handles) != world:
+            raise CklError(1, "IpcWindows", f"exchange returned {len(handles)} handles, not {world}")
+        self.ptrs, self._opened = [], []
+        for r, h in enumerate(handles):
+            if r == rank:
+                self.ptrs.append(self.own)
+            else:
+                p = ipc.open(h)
+                self.ptrs.append(p)
+                self._opened.append(p)
+
+    def _array(self):
+        return (C.c_void_p * EP_MAX_RANKS)(*(self.ptrs + [None] * (EP_MAX_RANKS - self.world)))
+
+    def close(self):
+        """Collective: unmaps the peers' windows, waits until every rank has done so (an
+        empty exchange), then frees the own window. No layer call may be in flight."""
+        for p in self._opened:
+            self._ipc.close(p)
+        self._opened = []
+        self._exchange(b"")
+        if self.own is not None:
+            self._ipc.free(self.own)
+            self.own = None
+
+
+class EpWindows(IpcWindows):
+    """The communication windows of an expert-parallel group (ckl_moe_ep_comm). All ranks
+    construct theirs collectively before any rank's first layer call."""
+
+    def __init__(self, rank, world, T_cap, k, E, d, exchange, ipc=_LibWindows):
+        if E % world:
+            raise CklError(2, "EpWindows", f"E={E} does not divide by world={world}")
+        nbytes = ep_window_bytes(world, T_cap, k, E, d) if ipc is _LibWindows else 0
+        super().__init__(rank, world, nbytes, exchange, ipc)
+        self.T_cap, self.k, self.E, self.d = T_cap, k, E, d
+        self.E_loc = E // world
+        self.comm = MoeEpComm(rank, world, T_cap, k, E, d, self._array())
+
+    def experts(self):
+        """Global expert ids owned by this rank."""
+        return range(self.rank * self.E_loc, (self.rank + 1) * self.E_loc)
+
+
+class GatherGroup(IpcWindows):
+    """Flag windows for gathers into one rank's buffers (ckl_peer_group): signal() on every
+    rank after its writes, wait() on the root before it reads."""
+
+    def __init__(self, rank, world, exchange, ipc=_LibWindows):
+        super().__init__(rank, world, PEER_WINDOW_BYTES, exchange, ipc)
+        self.group = PeerGroup(rank, world, self._array())
+
+    def signal(self, root=0, stream=None):
+        check(lib().ckl_gather_signal(C.byref(self.group), root, _stream(stream)),
+              "ckl_gather_signal")
+
+    def wait(self, stream=None):
+        check(lib().ckl_gather_wait(C.byref(self.group), _stream(stream)), "ckl_gather_wait")
+
+
+def decode_attention_gather(p: DecodeParams, out_full_ptr, lse_full_ptr, Hq_total, head_offset,
+                            workspace=None, stream=None):
+    """ckl_decode_attention_gather: this rank's head shard written into rows
+    [head_offset, head_offset + p.Hq) of a [B, Hq_total] output given by raw device
+    pointers (own or peer-mapped)."""
+    wsb = 0 if workspace is None else workspace.numel() * workspace.element_size()
+    check(lib().ckl_decode_attention_gather(C.byref(p), C.c_void_p(out_full_ptr),
+                                            C.c_void_p(lse_full_ptr), Hq_total, head_offset,
+                                            _ptr(workspace), wsb, _stream(stream)),
+          "ckl_decode_attention_gather")
+
+
+class MoeEpLayer:
+    """The expert-parallel SwiGLU MoE layer (ckl_moe_ep_layer): this rank's experts
+    gate/up [E/world][d][F], down [E/world][F][d]; forward() takes this rank's tokens."""
+
+    def __init__(self, windows: EpWindows, gate: QuantWeights, up: QuantWeights,
+                 down: QuantWeights):
+        self.win, self.gate, self.up, self.down = windows, gate, up, down
+
+    def workspace_size(self):
+        return lib().ckl_moe_ep_workspace_size(C.byref(self.win.comm), C.byref(self.gate.w),
+                                               C.byref(self.down.w))
+
+    def forward(self, logits, X, out=None, ids=None, wts=None, workspace=None, stream=None):
+        torch = _torch()
+        T = X.shape[0]
+        dev = X.device
+        if out is None:
+            out = torch.empty((T, self.win.d), dtype=torch.float16, device=dev)
+        need = self.workspace_size()
+        if workspace is None or workspace.numel() * workspace.element_size() < need:
+            workspace = torch.empty(need, dtype=torch.uint8, device=dev)
+        check(lib().ckl_moe_ep_layer(C.byref(self.win.comm), _ptr(logits), _ptr(X), T,
+                                     C.byref(self.gate.w), C.byref(self.up.w),
+                                     C.byref(self.down.w), _ptr(out), _ptr(ids), _ptr(wts),
+                                     _ptr(workspace), workspace.numel() * workspace.element_size(),
+                                     _stream(stream)), "ckl_moe_ep_layer")
         return out

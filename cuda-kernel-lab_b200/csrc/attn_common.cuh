@@ -55,8 +55,11 @@ inline ckl_status encode_kv_maps(const void* k_cache, const void* v_cache, int H
 
 // decode_attention.cu host helpers
 ckl_status validate(const ckl_decode_params* p, int* G);
+// out_heads / head_offset place direct-mode rows (b, h) at b*out_heads + head_offset + h
+// (out_heads 0 = Hq).
 ckl_status launch_partial(const ckl_decode_params* p, int G, bool direct, __half* out,
-                          float* lse, float* part_o, float* part_lse, cudaStream_t stream);
+                          float* lse, float* part_o, float* part_lse, cudaStream_t stream,
+                          int out_heads = 0, int head_offset = 0);
 size_t part_o_bytes(const ckl_decode_params* p);
 
 }  // namespace attn

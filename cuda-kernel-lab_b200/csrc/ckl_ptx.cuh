@@ -74,6 +74,32 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint64
     }
 }
 
+// ------------------------------------------------------------------ flags between GPUs
+// Release store / acquire load at system scope (the flag words of peer-mapped windows):
+// a writer's earlier stores (after a __threadfence_system()) are visible to a reader
+// that observed the flag.
+__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+// Waits until the epoch word at p has reached `epoch` (wrap-safe), giving up at `deadline`
+// (globaltimer ns) after recording DEVERR_TIMEOUT in *err. Returns false on timeout.
+__device__ __forceinline__ bool wait_epoch(const unsigned* p, unsigned epoch, uint64_t deadline,
+                                           unsigned* err) {
+    while ((int)(ld_acquire_sys(p) - epoch) < 0) {
+        if (globaltimer() > deadline) {
+            atomicOr(err, DEVERR_TIMEOUT);
+            return false;
+        }
+        __nanosleep(64);
+    }
+    return true;
+}
+
 // ------------------------------------------------------------------ programmatic dependent launch
 // Wait until the grids this one depends on (launched before it on the stream with the
 // programmatic-serialization attribute) have completed and their writes are visible; a no-op

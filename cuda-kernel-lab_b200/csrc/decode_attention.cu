@@ -52,6 +52,7 @@ struct Args {
     unsigned* err;
     unsigned long long timeout_ns;
     int B, Hq, Hkv, chunk_tokens, kv_start, chunk_base, part_stride, direct;
+    int out_heads, head_offset;   // direct mode: row (b, h) goes to out row b*out_heads + head_offset + h
     float scale_log2;
 };
 
@@ -304,8 +305,9 @@ decode_partial_kernel(const __grid_constant__ CUtensorMap tmK,
         const float lse_v = has ? (M + lg2(L)) * LN2 : -INFINITY;
         const size_t row = (size_t)b * a.Hq + (size_t)kvh * G + gq;
         if (a.direct) {
-            a.out[row * D + d] = __float2half_rn(val);
-            if (d == 0) a.lse[row] = lse_v;
+            const size_t orow = (size_t)b * a.out_heads + a.head_offset + (size_t)kvh * G + gq;
+            a.out[orow * D + d] = __float2half_rn(val);
+            if (d == 0) a.lse[orow] = lse_v;
         } else {
             const size_t slot = row * a.part_stride + a.chunk_base + chunk;
             a.part_o[slot * D + d] = val;
@@ -314,12 +316,17 @@ decode_partial_kernel(const __grid_constant__ CUtensorMap tmK,
     }
 }
 
-// LSE merge: one warp per (sequence, q head) row, 4 dims per lane (16-byte loads).
+// LSE merge: one warp per (sequence, q head) row, 4 dims per lane (16-byte loads). Row
+// r = b*Hq + h is written to out row b*out_heads + head_offset + h (identity when
+// out_heads = Hq and head_offset = 0; a head shard of a wider, possibly peer-mapped, output
+// otherwise).
 __global__ void __launch_bounds__(256)
 merge_states_kernel(const float* __restrict__ part_o, const float* __restrict__ part_lse,
-                    __half* __restrict__ out, float* __restrict__ lse_out, int rows, int slots) {
+                    __half* __restrict__ out, float* __restrict__ lse_out, int rows, int slots,
+                    int Hq, int out_heads, int head_offset) {
     const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (row >= rows) return;
+    const size_t orow = (size_t)(row / Hq) * out_heads + head_offset + row % Hq;
     const float* L = part_lse + (size_t)row * slots;
     float m = -INFINITY;
     for (int c = lane; c < slots; c += 32) m = fmaxf(m, L[c]);
@@ -345,8 +352,8 @@ merge_states_kernel(const float* __restrict__ part_o, const float* __restrict__ 
     uint2 pk;
     pk.x = *reinterpret_cast<uint32_t*>(&h0);
     pk.y = *reinterpret_cast<uint32_t*>(&h1);
-    reinterpret_cast<uint2*>(out + (size_t)row * D)[lane] = pk;
-    if (lane == 0) lse_out[row] = wsum > 0.f ? m + logf(wsum) : -INFINITY;
+    reinterpret_cast<uint2*>(out + orow * D)[lane] = pk;
+    if (lane == 0) lse_out[orow] = wsum > 0.f ? m + logf(wsum) : -INFINITY;
 }
 
 template <int G>
@@ -415,7 +422,8 @@ ckl_status validate(const ckl_decode_params* p, int* G) {
 }
 
 ckl_status launch_partial(const ckl_decode_params* p, int G, bool direct, __half* out,
-                          float* lse, float* part_o, float* part_lse, cudaStream_t stream) {
+                          float* lse, float* part_o, float* part_lse, cudaStream_t stream,
+                          int out_heads, int head_offset) {
     const DeviceInfo* di = device_info();
     if (!di) return CKL_CUDA_ERROR;
     const KernelSetup* ks = setup(di);
@@ -444,6 +452,8 @@ ckl_status launch_partial(const ckl_decode_params* p, int G, bool direct, __half
     a.chunk_base = p->chunk_base;
     a.part_stride = p->part_stride;
     a.direct = direct ? 1 : 0;
+    a.out_heads = out_heads > 0 ? out_heads : p->Hq;
+    a.head_offset = head_offset;
     a.scale_log2 = p->sm_scale * LOG2E;
 
     void* args[] = {&tmK, &tmV, &a};
@@ -517,30 +527,66 @@ ckl_status ckl_merge_states(const float* part_o, const float* part_lse, void* ou
     if (((uintptr_t)part_o & 15) || ((uintptr_t)out & 7))
         return fail(CKL_INVALID_ARG, "merge_states: part_o 16-byte / out 8-byte alignment");
     merge_states_kernel<<<ceil_div(rows, 8), 256, 0, (cudaStream_t)stream>>>(
-        part_o, part_lse, static_cast<__half*>(out), lse, rows, num_slots);
+        part_o, part_lse, static_cast<__half*>(out), lse, rows, num_slots, 1, 1, 0);
     CKL_CUDA_TRY(cudaGetLastError());
     return CKL_OK;
 }
 
-ckl_status ckl_decode_attention(const ckl_decode_params* p, void* out, float* lse,
-                                void* workspace, size_t workspace_bytes, void* stream) {
+}  // extern "C"
+
+namespace ckl {
+namespace attn {
+
+// decode_attention with the output rows of (b, h) at b*out_heads + head_offset + h.
+ckl_status decode_attention_rows(const ckl_decode_params* p, void* out, float* lse,
+                                 void* workspace, size_t workspace_bytes, cudaStream_t s,
+                                 int out_heads, int head_offset) {
     int G = 0;
     ckl_status st = validate(p, &G);
     if (st != CKL_OK || p->B == 0) return st;
     if (!out || !lse) return fail(CKL_INVALID_ARG, "out/lse are NULL");
-    const cudaStream_t s = (cudaStream_t)stream;
     if (p->num_chunks == 1 && p->chunk_base == 0 && p->part_stride == 1)
-        return launch_partial(p, G, true, static_cast<__half*>(out), lse, nullptr, nullptr, s);
+        return launch_partial(p, G, true, static_cast<__half*>(out), lse, nullptr, nullptr, s,
+                              out_heads, head_offset);
     const size_t need = ckl_decode_workspace_size(p);
     if (!workspace || workspace_bytes < need)
         return fail(CKL_WORKSPACE_TOO_SMALL, "decode_attention needs %zu workspace bytes, got %zu",
                     need, workspace_bytes);
     if ((uintptr_t)workspace & 255) return fail(CKL_INVALID_ARG, "workspace must be 256-byte aligned");
+    if ((uintptr_t)out & 7) return fail(CKL_INVALID_ARG, "out needs 8-byte alignment");
     float* part_o = static_cast<float*>(workspace);
     float* part_lse = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + part_o_bytes(p));
-    st = launch_partial(p, G, false, nullptr, nullptr, part_o, part_lse, s);
+    st = launch_partial(p, G, false, nullptr, nullptr, part_o, part_lse, s, 0, 0);
     if (st != CKL_OK) return st;
-    return ckl_merge_states(part_o, part_lse, out, lse, p->B * p->Hq, p->part_stride, stream);
+    const int rows = p->B * p->Hq;
+    merge_states_kernel<<<ceil_div(rows, 8), 256, 0, s>>>(part_o, part_lse,
+                                                          static_cast<__half*>(out), lse, rows,
+                                                          p->part_stride, p->Hq, out_heads,
+                                                          head_offset);
+    CKL_CUDA_TRY(cudaGetLastError());
+    return CKL_OK;
+}
+
+}  // namespace attn
+}  // namespace ckl
+
+extern "C" {
+
+ckl_status ckl_decode_attention(const ckl_decode_params* p, void* out, float* lse,
+                                void* workspace, size_t workspace_bytes, void* stream) {
+    return decode_attention_rows(p, out, lse, workspace, workspace_bytes, (cudaStream_t)stream,
+                                 p ? p->Hq : 0, 0);
+}
+
+ckl_status ckl_decode_attention_gather(const ckl_decode_params* p, void* out_full,
+                                       float* lse_full, int Hq_total, int head_offset,
+                                       void* workspace, size_t workspace_bytes, void* stream) {
+    if (!p) return fail(CKL_INVALID_ARG, "decode_attention_gather: params NULL");
+    if (Hq_total < p->Hq || head_offset < 0 || head_offset + p->Hq > Hq_total)
+        return fail(CKL_INVALID_ARG, "decode_attention_gather: heads [%d, %d) outside [0, %d)",
+                    head_offset, head_offset + p->Hq, Hq_total);
+    return decode_attention_rows(p, out_full, lse_full, workspace, workspace_bytes,
+                                 (cudaStream_t)stream, Hq_total, head_offset);
 }
 
 ckl_status ckl_validate_page_table(const int* h_indptr, const int* h_indices,

@@ -72,6 +72,7 @@ struct GemmArgs {
     const uint8_t* W1;        // up projection (SwiGLU)
     const __half* S1;
     void* Y;                  // [A, N] fp16 (or fp32 when y_f32), or fp32 split-K partials
+    const int* row_dst;       // [A] Y row of each permuted row (nullptr: row order kept)
     unsigned* err;
     unsigned long long timeout_ns;
     int E, K, N, ksplit, A, y_f32;
@@ -373,12 +374,14 @@ moe_gemm_kernel(const GemmArgs a) {
                     if (r >= nr || col >= a.N) continue;
                     float v0 = (acc0[i][c] + rw[(i * 4 + c) * RS]) * ((c & 2) ? pc0_hi : pc0_lo);
                     float v1 = SWIGLU ? (acc1[i][c] + rw[(TMAX * 4 + i * 4 + c) * RS]) * ((c & 2) ? pc1_hi : pc1_lo) : 0.f;
-                    const size_t o = (size_t)(row0 + r) * a.N + col;
                     if (a.ksplit > 1) {
+                        const size_t o = (size_t)(row0 + r) * a.N + col;
                         float* P = static_cast<float*>(a.Y) + (size_t)blockIdx.z * a.A * a.N * C::MATS;
                         P[o] = v0;
                         if (SWIGLU) P[(size_t)a.A * a.N + o] = v1;
                     } else {
+                        const int orow = a.row_dst ? __ldg(a.row_dst + row0 + r) : row0 + r;
+                        const size_t o = (size_t)orow * a.N + col;
                         float v = v0;
                         if (SWIGLU) {
                             v = v0 / (1.f + __expf(-v0)) * v1;
@@ -394,23 +397,29 @@ moe_gemm_kernel(const GemmArgs a) {
     }
 }
 
-// fixed-order sum of split-K partials; SwiGLU applies silu(gate) * up after the sum
+// Fixed-order sum of split-K partials [ksplit][A][N] (x2 for SwiGLU: gate then up); SwiGLU
+// applies silu(gate) * up after the sum. a_rows (device, optional) is the number of rows in
+// use (<= A); row_dst (optional) maps row r to output row row_dst[r].
 template <bool SWIGLU>
-__global__ void splitk_reduce_kernel(const float* __restrict__ P, void* Y, int y_f32, size_t n,
-                                     int ksplit) {
+__global__ void splitk_reduce_kernel(const float* __restrict__ P, void* Y, int y_f32, int A, int N,
+                                     int ksplit, const int* __restrict__ row_dst,
+                                     const int* __restrict__ a_rows) {
     pdl_wait();
     pdl_trigger();
-    const size_t stride = SWIGLU ? 2 * n : n;
+    const size_t n_all = (size_t)A * N;
+    const size_t n = a_rows ? (size_t)min(A, __ldg(a_rows)) * N : n_all;
+    const size_t stride = SWIGLU ? 2 * n_all : n_all;
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
          i += (size_t)gridDim.x * blockDim.x) {
         float s = 0.f, u = 0.f;
         for (int z = 0; z < ksplit; z++) {
             s += P[z * stride + i];
-            if (SWIGLU) u += P[z * stride + n + i];
+            if (SWIGLU) u += P[z * stride + n_all + i];
         }
         if (SWIGLU) s = __half2float(__float2half_rn(s / (1.f + __expf(-s)) * u));
-        if (y_f32) static_cast<float*>(Y)[i] = s;
-        else static_cast<__half*>(Y)[i] = __float2half_rn(s);
+        const size_t o = row_dst ? (size_t)__ldg(row_dst + i / N) * N + i % N : i;
+        if (y_f32) static_cast<float*>(Y)[o] = s;
+        else static_cast<__half*>(Y)[o] = __float2half_rn(s);
     }
 }
 
@@ -654,7 +663,7 @@ namespace moe {
 ckl_status expert_gemm(const void* X, const int* row_src, const int* offsets, int A, int max_rows,
                        const ckl_moe_weights* w0, const ckl_moe_weights* w1, void* Y, int y_f32,
                        int force_ksplit, void* workspace, size_t workspace_bytes, void* stream,
-                       int dep = 0);
+                       int dep = 0, const int* row_dst = nullptr, const int* a_rows = nullptr);
 }  // namespace moe
 }  // namespace ckl
 
@@ -738,7 +747,7 @@ namespace moe {
 ckl_status expert_gemm(const void* X, const int* row_src, const int* offsets, int A, int max_rows,
                        const ckl_moe_weights* w0, const ckl_moe_weights* w1, void* Y, int y_f32,
                        int force_ksplit, void* workspace, size_t workspace_bytes, void* stream,
-                       int dep) {
+                       int dep, const int* row_dst, const int* a_rows) {
     ckl_status st = check_weights(w0, "moe_expert_gemm");
     if (st != CKL_OK) return st;
     const bool swiglu = w1 != nullptr;
@@ -776,6 +785,7 @@ ckl_status expert_gemm(const void* X, const int* row_src, const int* offsets, in
     a.W1 = swiglu ? static_cast<const uint8_t*>(w1->packed) : nullptr;
     a.S1 = swiglu ? static_cast<const __half*>(w1->scales) : nullptr;
     a.Y = ks > 1 ? workspace : Y;
+    a.row_dst = row_dst;
     a.err = di->err_word;
     a.timeout_ns = spin_timeout_ns();
     a.E = w0->E;
@@ -791,10 +801,9 @@ ckl_status expert_gemm(const void* X, const int* row_src, const int* offsets, in
     const cudaStream_t s = (cudaStream_t)stream;
     CKL_CUDA_TRY(launch(v.fn, grid, dim3(GTHREADS), v.smem, s, args, dep != 0));
     if (ks > 1) {
-        size_t n = (size_t)A * w0->N;
         const float* P = static_cast<const float*>(workspace);
-        int ksv = ks;
-        void* rargs[] = {&P, &Y, &y_f32, &n, &ksv};
+        int ksv = ks, Av = A, Nv = w0->N;
+        void* rargs[] = {&P, &Y, &y_f32, &Av, &Nv, &ksv, &row_dst, &a_rows};
         const void* rfn = swiglu ? reinterpret_cast<const void*>(splitk_reduce_kernel<true>)
                                  : reinterpret_cast<const void*>(splitk_reduce_kernel<false>);
         CKL_CUDA_TRY(launch(rfn, dim3(256), dim3(256), 0, s, rargs, dep != 0));

@@ -29,7 +29,7 @@ namespace moe {
 ckl_status expert_gemm(const void* X, const int* row_src, const int* offsets, int A, int max_rows,
                        const ckl_moe_weights* w0, const ckl_moe_weights* w1, void* Y, int y_f32,
                        int force_ksplit, void* workspace, size_t workspace_bytes, void* stream,
-                       int dep);
+                       int dep, const int* row_dst = nullptr, const int* a_rows = nullptr);
 
 constexpr int MAX_E = 256;
 constexpr int MAX_K = 8;
@@ -210,6 +210,17 @@ ckl_status route_setup() {
         st[di->device] = cuda_status(e, "routing kernel setup");
     });
     return st[di->device];
+}
+
+// Routing of T tokens (T may be 0: counts and offsets are then all zero).
+ckl_status route_tokens(const float* logits, int T, int E, int k, int* ids, float* wts,
+                        int* counts, int* offsets, int* inv_perm, int* row_src, cudaStream_t s) {
+    ckl_status st = route_setup();
+    if (st != CKL_OK) return st;
+    route_kernel<<<1, ROUTE_THREADS, route_smem(T, E), s>>>(logits, T, E, k, ids, wts, counts,
+                                                            offsets, inv_perm, row_src, 1, nullptr);
+    CKL_CUDA_TRY(cudaGetLastError());
+    return CKL_OK;
 }
 
 ckl_status check_route(int T, int E, int k) {

@@ -290,6 +290,94 @@ CKL_API ckl_status ckl_moe_layer(const float* logits, const void* X, int T, int 
                                  void* stream);
 
 /* ======================================================================================
+ * Head-parallel decode attention with a fused gather (north star: attention partitioned by
+ * KV head, "no collective except a final gather"; the reference is single-GPU)
+ * ==================================================================================== */
+
+/* ckl_decode_attention for one KV-head shard: p describes this rank's heads (Hq, Hkv, its
+ * q [B,Hq,128], K/V pages [num_pages,16,Hkv,128] holding only its heads; the page table is
+ * the replicated one), and the rows of (b, h) are written to out_full[b][head_offset + h]
+ * and lse_full[b][head_offset + h] of a [B][Hq_total] output -- which may be another GPU's
+ * buffer mapped into this process (CUDA IPC): the kernel that produces a row stores it
+ * over NVLink, so the gather needs no copy or collective of its own. */
+CKL_API ckl_status ckl_decode_attention_gather(const ckl_decode_params* p, void* out_full,
+                                               float* lse_full, int Hq_total, int head_offset,
+                                               void* workspace, size_t workspace_bytes,
+                                               void* stream);
+
+/* A group of ranks with a small peer-mapped flag window each (CKL_PEER_WINDOW_BYTES,
+ * allocated with ckl_ep_window_alloc and mapped with ckl_ep_window_open). */
+#define CKL_PEER_WINDOW_BYTES 256
+typedef struct ckl_peer_group {
+    int rank, world;
+    void* windows[8];    /* windows[i] = rank i's flag window as mapped here */
+} ckl_peer_group;
+
+/* Completion of a gather into `root`: every rank calls ckl_gather_signal after the calls
+ * that write into the root's buffers (stream order); the root calls ckl_gather_wait before
+ * it reads them. Epoch flags, bounded wait (CKL_TIMEOUT via ckl_check_device_error). Every
+ * rank signals once per root wait. */
+CKL_API ckl_status ckl_gather_signal(const ckl_peer_group* g, int root, void* stream);
+CKL_API ckl_status ckl_gather_wait(const ckl_peer_group* g, void* stream);
+
+/* ======================================================================================
+ * Expert-parallel MoE layer over NVLink peer memory (north star: "expert-parallel with a
+ * token all-to-all for dispatch and combine"; the reference is single-GPU and has no
+ * counterpart -- its layer is MoeDecode, 03_moe_wq_decode.cu:350-391)
+ * ==================================================================================== */
+
+#define CKL_EP_MAX_RANKS 8
+#define CKL_IPC_HANDLE_BYTES 64
+
+/* Rank r owns experts [r*E/world, (r+1)*E/world). Every rank has a communication window
+ * (one device allocation of ckl_moe_ep_window_bytes) that every other rank maps:
+ *   dispatch: each rank routes its own T tokens and writes the token row of every
+ *             (token, slot) assignment into the owner's window, in slab `rank`, at the
+ *             assignment's position among this rank's rows for that owner (expert order);
+ *   experts:  the owner runs the gate/up and down GEMMs over the rows it received
+ *             (its local experts, packed like any ckl_moe_weights with E = E/world);
+ *   combine:  every rank reads its assignments' outputs back from the owners' windows and
+ *             sums them in fixed slot order (as ckl_moe_combine).
+ * Ranks are kept in step by epoch flags in the windows (release/acquire at system scope)
+ * with bounded waits; a wait that gives up records CKL_TIMEOUT (ckl_check_device_error). */
+typedef struct ckl_moe_ep_comm {
+    int rank, world;       /* world <= CKL_EP_MAX_RANKS, E % world == 0 */
+    int T_cap;             /* most tokens any rank passes in one call */
+    int k, E, d;           /* top-k, total experts, d_model (row width) */
+    void* windows[CKL_EP_MAX_RANKS];   /* windows[i] = rank i's window as mapped here
+                                          (windows[rank] = this rank's own) */
+} ckl_moe_ep_comm;
+
+/* Bytes of one rank's window for this configuration. */
+CKL_API size_t ckl_moe_ep_window_bytes(int world, int T_cap, int k, int E, int d);
+
+/* Window allocation helpers (CUDA IPC; the caller owns the memory): alloc zeroes a window
+ * on the current device and returns its IPC handle (CKL_IPC_HANDLE_BYTES bytes) for the
+ * other ranks (alloc returns after the window is zeroed); open maps a peer's handle;
+ * close unmaps; free releases an own window. Every rank must have allocated its window
+ * before any rank's first ckl_moe_ep_layer (a host barrier after alloc), and every peer
+ * must have closed its mapping before the owner frees it (a host barrier between). */
+CKL_API ckl_status ckl_ep_window_alloc(size_t bytes, void** window, void* ipc_handle);
+CKL_API ckl_status ckl_ep_window_open(const void* ipc_handle, void** window);
+CKL_API ckl_status ckl_ep_window_close(void* window);
+CKL_API ckl_status ckl_ep_window_free(void* window);
+
+/* Workspace of ckl_moe_ep_layer on this rank (gate/down: this rank's local experts). */
+CKL_API size_t ckl_moe_ep_workspace_size(const ckl_moe_ep_comm* comm, const ckl_moe_weights* gate,
+                                         const ckl_moe_weights* down);
+
+/* One expert-parallel SwiGLU MoE layer. Every rank calls it the same number of times, with
+ * its own T (0 <= T <= T_cap) tokens: logits fp32 [T][E], X fp16 [T][d], out fp16 [T][d];
+ * gate/up [E/world][d][F] and down [E/world][F][d] are this rank's experts. ids_out /
+ * wts_out (optional, [T][k]) receive the routing. Asynchronous, no host sync; the result
+ * equals ckl_moe_layer over all E experts up to the split-K summation order. */
+CKL_API ckl_status ckl_moe_ep_layer(const ckl_moe_ep_comm* comm, const float* logits,
+                                    const void* X, int T, const ckl_moe_weights* gate,
+                                    const ckl_moe_weights* up, const ckl_moe_weights* down,
+                                    void* out, int* ids_out, float* wts_out, void* workspace,
+                                    size_t workspace_bytes, void* stream);
+
+/* ======================================================================================
  * Measurement
  * ==================================================================================== */
 

@@ -391,3 +391,34 @@ def port_attention_seconds(bt, threads):
     t0 = time.perf_counter()
     attention_ref(bt, threads=threads)
     return time.perf_counter() - t0
+
+
+# ------------------------------------------------------------------ expert parallelism
+# Restatement, for the tests, of where the expert-parallel layer (ckl_moe_ep_layer) puts
+# rows. The reference is single-GPU; its layer (MoeDecode, 03_moe_wq_decode.cu:350-391) is
+# the oracle the partitioned result is compared with.
+def ep_dispatch(ids, inv_perm, offsets, E_loc):
+    """Owner rank and slab position of every assignment i = t*k + j of one rank's tokens:
+    owner = ids[i] // E_loc, pos = inv_perm[i] - offsets[owner * E_loc] (expert order
+    within the rank's slab on the owner)."""
+    ids = np.asarray(ids, np.int64).reshape(-1)
+    owner = ids // E_loc
+    pos = np.asarray(inv_perm, np.int64) - np.asarray(offsets, np.int64)[owner * E_loc]
+    return owner, pos
+
+
+def ep_receive(counts_from, cap):
+    """counts_from [world][E_loc] (rows source s sent for each local expert) -> the expert
+    offsets [E_loc + 1] over all received rows and the gather map row_src[a] = s*cap + slab
+    position, ordered by expert, then source, then slab position."""
+    counts_from = np.asarray(counts_from, np.int64)
+    world, E_loc = counts_from.shape
+    soff = np.zeros_like(counts_from)
+    soff[:, 1:] = np.cumsum(counts_from, axis=1)[:, :-1]
+    offsets = np.zeros(E_loc + 1, np.int64)
+    offsets[1:] = np.cumsum(counts_from.sum(axis=0))
+    row_src = []
+    for e in range(E_loc):
+        for s in range(world):
+            row_src.extend(range(s * cap + soff[s, e], s * cap + soff[s, e] + counts_from[s, e]))
+    return offsets.astype(np.int32), np.asarray(row_src, np.int32)

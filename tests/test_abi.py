@@ -78,10 +78,9 @@ def test_invalid_params_rejected_before_any_launch(ckl):
 
 
 def test_no_fallback_when_library_missing(tmp_path, monkeypatch):
-    import importlib
     import ckl as m
     monkeypatch.setattr(m, "LIB_PATH", str(tmp_path / "missing.so"))
     monkeypatch.setattr(m, "_lib", None)
     with pytest.raises(m.CklError):
         m.lib()
-    importlib.reload(m)
+    # monkeypatch restores the loaded library (and its bound signatures) afterwards
