@@ -8,8 +8,11 @@ One step = one ckl_decode_attention call (the C-ABI entry point; partial kernel 
 merge when the batch is split) over one synthetic paged batch: Hq=32, Hkv=8, d=128, page
 16, shuffled page table, K/V U(-1,1) fp16 filled on the device. The default workload is
 B=256 x L=4096 (4.3 GB of KV, larger than the 126 MB L2, so no flush is needed between
-steps). Under torchrun (N>1) every rank decodes its own batch of the same shape (weak
-scaling by sequence; no collective on the data path); timing is CUDA events, max over ranks.
+steps). Under torchrun (N>1) the KV heads are sharded N ways and the batch grows to
+B = 256*N sequences, so every GPU streams the single-GPU workload's KV bytes (weak
+scaling); each GPU's decode kernels store its output rows straight into rank 0's output
+over NVLink (the gather), and rank 0 waits on per-rank epoch flags before the step ends.
+Timing is CUDA events, max over ranks.
 
 Rank 0 prints one JSON line. `value` = algorithmic bytes of all ranks / max step time
 (sum of K+V of every token + q + out + lse); `e2e` = the same metric with the per-step
@@ -72,12 +75,22 @@ def algorithmic_bytes(lens):
 
 
 def config_of(workload, lens, n):
-    return {"workload": f"paged GQA decode attention {workload}", "B": int(len(lens)),
-            "L": "U[128,8192]" if WORKLOADS[workload]["L"] is None else int(lens[0]),
-            "Hq": HQ, "Hkv": HKV, "head_dim": D, "page": PAGE, "page_table": "shuffled",
-            "kv_dtype": "fp16", "per_rank": "own batch (weak scaling by sequence)",
-            "l2": "inputs larger than L2 (KV %.2f GB > 126 MB), no flush" %
-                  (algorithmic_bytes(lens) / 1e9), "parallelism": f"replicas x{n}"}
+    c = {"workload": f"paged GQA decode attention {workload}", "B": int(len(lens)),
+         "L": "U[128,8192]" if WORKLOADS[workload]["L"] is None else int(lens[0]),
+         "Hq": HQ, "Hkv": HKV, "head_dim": D, "page": PAGE, "page_table": "shuffled",
+         "kv_dtype": "fp16",
+         "l2": "inputs larger than L2 (KV %.2f GB per GPU > 126 MB), no flush" %
+               (algorithmic_bytes(lens) / 1e9 / n)}
+    if n == 1:
+        c["parallelism"] = "single GPU"
+    else:
+        c["parallelism"] = (f"KV heads sharded {n} ways ({HKV // n} KV / {HQ // n} q heads per "
+                            "GPU), page table replicated; each GPU's output rows stored into "
+                            "rank 0's output by the decode kernels (fused gather) + epoch-flag "
+                            "completion wait on rank 0")
+        c["per_gpu"] = (f"weak scaling: B = {len(lens) // n} x {n} sequences, so every GPU "
+                        "streams the KV bytes of the single-GPU workload")
+    return c
 
 
 # ------------------------------------------------------------------ clocks
@@ -281,11 +294,14 @@ def _fill_uniform(t, g):
 
 class ColdTimer:
     """Median CUDA-event time of fn with L2 overwritten (256 MB memset, > 2x L2) before
-    every sample, as the reference's Bench::time_cold (common/bench.cuh:111-131)."""
+    every sample, as the reference's Bench::time_cold (common/bench.cuh:111-131). With
+    world > 1 every rank calls it: the ranks start each sample together (host barrier after
+    the flush) and the result is the max over ranks of the per-rank medians."""
 
-    def __init__(self, dev):
+    def __init__(self, dev, world=1):
         import torch
         self.flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+        self.world = world
 
     def __call__(self, fn, iters=15, warmup=3):
         import torch
@@ -296,13 +312,15 @@ class ColdTimer:
         ts = []
         for i in range(iters):
             self.flush.fill_(i & 0xFF)
+            if self.world > 1:
+                barrier(self.world)
             e0.record()
             fn()
             e1.record()
             e1.synchronize()
             ts.append(e0.elapsed_time(e1))
         ts.sort()
-        return ts[len(ts) // 2]
+        return max_over_ranks(ts[len(ts) // 2], self.world)
 
 
 def paged_batch(lens, dev, seed, Lp=0):
@@ -534,6 +552,150 @@ def bench_mixtral_layer(ckl, dev, timer, peak):
     return res
 
 
+def _split(T, world, rank):
+    return T // world + (1 if rank < T % world else 0)
+
+
+def bench_moe_ep(ckl, dev, timer, peak, rank, world, exchange, n_layers=8):
+    """BASELINE config 4 expert-parallel: experts [r*E/n, (r+1)*E/n) on GPU r, tokens routed
+    on their own GPU and exchanged through IPC-mapped windows by the layer's kernels
+    (ckl_moe_ep_layer). Same methodology as the single-GPU figure: n_layers layers with
+    distinct weights in one CUDA graph, L2 flushed before every replay, per-layer time, max
+    over ranks. T is the layer's whole batch split over the GPUs (the single-GPU config);
+    "T=64/GPU" keeps 64 tokens on every GPU."""
+    import numpy as np
+    import torch
+    E, k, d, F, T_cap = 64, 6, 2048, 1408, 64
+    E_loc = E // world
+    g = torch.Generator(device=dev)
+    g.manual_seed(4400 + rank)
+    mk = lambda *sh: (torch.randn(*sh, generator=g, device=dev) * 0.02).half()
+    win = ckl.EpWindows(rank, world, T_cap, k, E, d, exchange)
+    layers = []
+    for _ in range(n_layers):
+        q = [ckl.QuantWeights(4, mk(E_loc, d, F), group=128, asym=True) for _ in range(2)]
+        q.append(ckl.QuantWeights(4, mk(E_loc, F, d), group=128, asym=True))
+        layers.append((q, ckl.MoeEpLayer(win, *q)))
+    ws = torch.empty(layers[0][1].workspace_size(), dtype=torch.uint8, device=dev)
+    res = {}
+    for name, T in [("T=1", 1), ("T=4", 4), ("T=16", 16), ("T=64", 64), ("T=64/GPU", 64 * world)]:
+        Tr = _split(T, world, rank)
+        lg = [torch.randn((max(Tr, 1), E), generator=g, device=dev)[:Tr].contiguous()
+              for _ in range(n_layers)]
+        X = torch.randn((max(Tr, 1), d), generator=g, device=dev).half()[:Tr].contiguous()
+        outs = [torch.empty((Tr, d), dtype=torch.float16, device=dev) for _ in range(n_layers)]
+        ids = [torch.empty((Tr, k), dtype=torch.int32, device=dev) for _ in range(n_layers)]
+
+        def step():
+            x = X
+            for l, (_, layer) in enumerate(layers):
+                layer.forward(lg[l], x, out=outs[l], ids=ids[l], workspace=ws)
+                x = outs[l]
+
+        t = timer(GraphStep(step, dev)) / n_layers
+        # algorithmic bytes: the local experts that received rows, summed over the GPUs
+        act = []
+        for l in range(n_layers):
+            e_all = [None] * world
+            import torch.distributed as dist
+            dist.all_gather_object(e_all, ids[l].cpu().numpy().ravel().tolist())
+            act.append(len(set(sum(e_all, []))))
+        per_exp = sum(w.bytes_per_expert() for w in layers[0][0])
+        byts = per_exp * sum(act) / n_layers + T * d * 2 * 2
+        res[name] = {"us_per_layer": round(t * 1e3, 2), "tokens_per_gpu": Tr,
+                     "active_experts_avg": round(sum(act) / n_layers, 1),
+                     "bytes_per_layer_all_gpus": int(byts),
+                     "GB/s_all_gpus": round(byts / (t * 1e-3) / 1e9, 1),
+                     "frac_of_measured_hbm_all_gpus": round(byts / (t * 1e-3) / 1e9 / (peak * world), 3)}
+    res["method"] = (f"{n_layers} layers with distinct weights ({E_loc} experts each per GPU) in "
+                     "one CUDA graph per GPU, L2 flushed before each replay, per-layer time, max "
+                     "over GPUs; dispatch/combine by the layer's kernels over NVLink (no NCCL)")
+    torch.cuda.synchronize()
+    del layers
+    win.close()
+    torch.cuda.empty_cache()
+    return res
+
+
+def bench_mixtral_ep(ckl, dev, timer, peak, rank, world, exchange):
+    """BASELINE config 5 on several GPUs: attention of B=32 sequences of 4096 with the KV
+    heads sharded over the GPUs (each GPU decodes its 8/n KV heads for all sequences), then
+    the MoE block (E=8, top-2, d=4096, F=14336, int8 per channel) expert-parallel with the
+    T=32 tokens split over the GPUs. One step = attention + MoE from one CUDA graph, cold L2,
+    max over GPUs. (The o_proj GEMM and its reduce-scatter between them are outside the
+    reference's layer and not run.)"""
+    import numpy as np
+    import torch
+    B, L = 32, 4096
+    E, k, d, F = 8, 2, 4096, 14336
+    hk = HKV // world
+    lens = np.full(B, L, np.int32)
+    npg = (lens + PAGE - 1) // PAGE
+    indptr = np.zeros(B + 1, np.int32)
+    indptr[1:] = np.cumsum(npg)
+    last = (lens - (npg - 1) * PAGE).astype(np.int32)
+    indices = np.random.default_rng(55).permutation(int(indptr[-1])).astype(np.int32)
+    g = torch.Generator(device=dev)
+    g.manual_seed(5500 + rank)
+    kc = torch.empty((int(indptr[-1]), PAGE, hk, D), dtype=torch.float16, device=dev)
+    vc = torch.empty_like(kc)
+    _fill_uniform(kc, g)
+    _fill_uniform(vc, g)
+    t_ = lambda a: torch.from_numpy(a).to(dev)
+    d_attn = dict(q=(torch.rand((B, HQ // world, D), generator=g, device=dev) * 2 - 1).half(),
+                  k_cache=kc, v_cache=vc, kv_indptr=t_(indptr), kv_indices=t_(indices),
+                  kv_last_page_len=t_(last))
+    nc, ct = ckl.plan_chunks(HQ // HKV, B, hk, L)
+    pa = ckl.make_params(**d_attn, num_chunks=nc, chunk_tokens=ct)
+    a_out = torch.empty_like(d_attn["q"])
+    a_lse = torch.empty((B, HQ // world), dtype=torch.float32, device=dev)
+    a_ws = torch.empty(max(ckl.workspace_size(pa), 256), dtype=torch.uint8, device=dev)
+    mk = lambda *sh: (torch.randn(*sh, generator=g, device=dev) * 0.02).half()
+    E_loc = E // world
+    q = [ckl.QuantWeights(8, mk(E_loc, d, F), group=d), ckl.QuantWeights(8, mk(E_loc, d, F), group=d),
+         ckl.QuantWeights(8, mk(E_loc, F, d), group=F)]
+    Tr = _split(B, world, rank)
+    win = ckl.EpWindows(rank, world, (B + world - 1) // world, k, E, d, exchange)
+    layer = ckl.MoeEpLayer(win, *q)
+    lg = torch.randn((max(Tr, 1), E), generator=g, device=dev)[:Tr].contiguous()
+    X = torch.randn((max(Tr, 1), d), generator=g, device=dev).half()[:Tr].contiguous()
+    out = torch.empty((Tr, d), dtype=torch.float16, device=dev)
+    ids = torch.empty((Tr, k), dtype=torch.int32, device=dev)
+    ws = torch.empty(layer.workspace_size(), dtype=torch.uint8, device=dev)
+
+    def attn():
+        ckl.decode_attention(**d_attn, num_chunks=nc, chunk_tokens=ct, out=a_out, lse=a_lse,
+                             workspace=a_ws)
+
+    def moe():
+        layer.forward(lg, X, out=out, ids=ids, workspace=ws)
+
+    def step():
+        attn()
+        moe()
+
+    t_attn = timer(GraphStep(attn, dev))
+    t_moe = timer(GraphStep(moe, dev))
+    t_step = timer(GraphStep(step, dev))
+    import torch.distributed as dist
+    e_all = [None] * world
+    dist.all_gather_object(e_all, ids.cpu().numpy().ravel().tolist())
+    active = len(set(sum(e_all, [])))
+    attn_bytes = algorithmic_bytes(lens)
+    moe_bytes = active * sum(w.bytes_per_expert() for w in q) + B * d * 2 * 2
+    res = {"us_step": round(t_step * 1e3, 2), "us_attention": round(t_attn * 1e3, 2),
+           "us_moe": round(t_moe * 1e3, 2), "attention_bytes_all_gpus": attn_bytes,
+           "moe_bytes_all_gpus": moe_bytes, "moe_active_experts": active,
+           "GB/s_step_all_gpus": round((attn_bytes + moe_bytes) / (t_step * 1e-3) / 1e9, 1),
+           "frac_of_measured_hbm_all_gpus":
+               round((attn_bytes + moe_bytes) / (t_step * 1e-3) / 1e9 / (peak * world), 3)}
+    torch.cuda.synchronize()
+    del layer, q, d_attn
+    win.close()
+    torch.cuda.empty_cache()
+    return res
+
+
 # ------------------------------------------------------------------ our arm
 def run_ours(args):
     import numpy as np
@@ -542,49 +704,69 @@ def run_ours(args):
 
     rank, world, local = dist_setup(args.gpus)
     dev = torch.device("cuda", local)
-    lens = lengths(args.workload)
+    if HKV % world:
+        sys.exit(f"--gpus {world}: the {HKV} KV heads do not shard {world} ways")
+    hk, hq = HKV // world, HQ // world              # this GPU's KV / q heads
+    lens = np.tile(lengths(args.workload), world)    # weak scaling: B grows with the GPUs
     B = len(lens)
     npg = (lens + PAGE - 1) // PAGE
     indptr = np.zeros(B + 1, np.int32)
     indptr[1:] = np.cumsum(npg)
     last = (lens - (npg - 1) * PAGE).astype(np.int32)
     num_pages = int(indptr[-1])
-    rng = np.random.default_rng(1000 + rank)
+    rng = np.random.default_rng(1000)                # the page table is replicated
     indices = rng.permutation(num_pages).astype(np.int32)
 
     g = torch.Generator(device=dev)
     g.manual_seed(1000 + rank)
-    k = torch.empty((num_pages, PAGE, HKV, D), dtype=torch.float16, device=dev)
+    k = torch.empty((num_pages, PAGE, hk, D), dtype=torch.float16, device=dev)
     v = torch.empty_like(k)
-    for t in (k, v):   # chunked U(-1,1) fill keeps the fp32 temporary small
-        flat = t.view(-1)
-        step = 1 << 28
-        for s0 in range(0, flat.numel(), step):
-            n = min(step, flat.numel() - s0)
-            flat[s0:s0 + n] = (torch.rand(n, generator=g, device=dev) * 2 - 1).half()
-    q_host = (torch.rand((B, HQ, D), generator=g, device=dev) * 2 - 1).half().cpu().pin_memory()
+    _fill_uniform(k, g)
+    _fill_uniform(v, g)
+    q_host = (torch.rand((B, hq, D), generator=g, device=dev) * 2 - 1).half().cpu().pin_memory()
     d_q = q_host.to(dev)
     d_indptr = torch.from_numpy(indptr).to(dev)
     d_indices = torch.from_numpy(indices).to(dev)
     d_last = torch.from_numpy(last).to(dev)
-    nc, ct = ckl.plan_chunks(HQ // HKV, B, HKV, int(lens.max()))
+    nc, ct = ckl.plan_chunks(HQ // HKV, B, hk, int(lens.max()))
     p = ckl.make_params(d_q, k, v, d_indptr, d_indices, d_last, num_chunks=nc, chunk_tokens=ct)
-    out = torch.empty_like(d_q)
-    lse = torch.empty((B, HQ), dtype=torch.float32, device=dev)
     ws_n = ckl.workspace_size(p)
     ws = torch.empty(max(ws_n, 256), dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream()
-    launches_per_step = 1 if nc == 1 else 2
-    byts = algorithmic_bytes(lens)
+    byts = algorithmic_bytes(lens) // world          # this GPU's share (its heads)
 
     import ctypes as C
     L = ckl.lib()
     sptr = C.c_void_p(stream.cuda_stream)
+    if world == 1:
+        out = torch.empty((B, HQ, D), dtype=torch.float16, device=dev)
+        lse = torch.empty((B, HQ), dtype=torch.float32, device=dev)
+        out_ptr, lse_ptr, win, grp = out.data_ptr(), lse.data_ptr(), None, None
+        launches_per_step = 1 if nc == 1 else 2
+    else:
+        # rank 0's output [B, Hq, 128] + lse lives in an IPC window every rank maps
+        ex = ckl.torch_exchange()
+        out_bytes = (B * HQ * D * 2 + 255) // 256 * 256
+        win = ckl.IpcWindows(rank, world, out_bytes + B * HQ * 4, ex)
+        grp = ckl.GatherGroup(rank, world, ex)
+        out_ptr, lse_ptr = win.ptrs[0], win.ptrs[0] + out_bytes
+        out = ckl.device_view(win.ptrs[rank], (B, HQ, D), torch.float16) if rank == 0 else None
+        lse = ckl.device_view(win.ptrs[rank] + out_bytes, (B, HQ), torch.float32) if rank == 0 else None
+        launches_per_step = (1 if nc == 1 else 2) + 1 + (1 if rank == 0 else 0)
 
     def step():
-        ckl.check(L.ckl_decode_attention(C.byref(p), C.c_void_p(out.data_ptr()),
-                                         C.c_void_p(lse.data_ptr()), C.c_void_p(ws.data_ptr()),
-                                         ws.numel(), sptr), "ckl_decode_attention")
+        if world == 1:
+            ckl.check(L.ckl_decode_attention(C.byref(p), C.c_void_p(out_ptr),
+                                             C.c_void_p(lse_ptr), C.c_void_p(ws.data_ptr()),
+                                             ws.numel(), sptr), "ckl_decode_attention")
+            return
+        ckl.check(L.ckl_decode_attention_gather(C.byref(p), C.c_void_p(out_ptr),
+                                                C.c_void_p(lse_ptr), HQ, rank * hq,
+                                                C.c_void_p(ws.data_ptr()), ws.numel(), sptr),
+                  "ckl_decode_attention_gather")
+        grp.signal(0, stream)
+        if rank == 0:
+            grp.wait(stream)
 
     # ---- device-resident timing (value)
     for _ in range(args.warmup):
@@ -610,7 +792,7 @@ def run_ours(args):
     else:
         pp = ckl.make_params(d_q, k, v, d_indptr, d_indices, d_last, num_chunks=nc,
                              chunk_tokens=ct)
-        po_bytes = ((B * HQ * nc * D * 4 + 255) // 256) * 256   # workspace layout
+        po_bytes = ((B * hq * nc * D * 4 + 255) // 256) * 256   # workspace layout
         pp.part_o = ws.data_ptr()
         pp.part_lse = ws.data_ptr() + po_bytes
         for _ in range(3):
@@ -623,14 +805,15 @@ def run_ours(args):
         torch.cuda.synchronize()
         kern_ms = e0.elapsed_time(e1) / args.steps
 
-    # ---- end to end through the C-ABI with host buffers
+    # ---- end to end through the C-ABI with host buffers (every GPU copies its q shard and
+    # the page table in; rank 0 reads the gathered output and lse back)
     h_indptr = torch.from_numpy(indptr).pin_memory()
     h_indices = torch.from_numpy(indices).pin_memory()
     h_last = torch.from_numpy(last).pin_memory()
-    h_out = torch.empty((B, HQ, D), dtype=torch.float16).pin_memory()
-    h_lse = torch.empty((B, HQ), dtype=torch.float32).pin_memory()
+    h_out = torch.empty((B, HQ, D), dtype=torch.float16).pin_memory() if rank == 0 else None
+    h_lse = torch.empty((B, HQ), dtype=torch.float32).pin_memory() if rank == 0 else None
     h2d = q_host.numel() * 2 + h_indptr.numel() * 4 + h_indices.numel() * 4 + h_last.numel() * 4
-    d2h = h_out.numel() * 2 + h_lse.numel() * 4
+    d2h = B * HQ * D * 2 + B * HQ * 4 if rank == 0 else 0
 
     def e2e_step():
         d_q.copy_(q_host, non_blocking=True)
@@ -638,8 +821,9 @@ def run_ours(args):
         d_indices.copy_(h_indices, non_blocking=True)
         d_last.copy_(h_last, non_blocking=True)
         step()
-        h_out.copy_(out, non_blocking=True)
-        h_lse.copy_(lse, non_blocking=True)
+        if rank == 0:
+            h_out.copy_(out, non_blocking=True)
+            h_lse.copy_(lse, non_blocking=True)
 
     for _ in range(args.warmup):
         e2e_step()
@@ -651,28 +835,44 @@ def run_ours(args):
     barrier(world)
     e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, world)
 
-    # correctness of what was timed: a sampled sequence against a plain fp32 torch check
-    b0 = 0
+    # correctness of what was timed: the last sequence's rows, read from the (gathered)
+    # output on rank 0, against a plain fp32 torch check that every GPU computes for its own
+    # heads from its own K/V shard (torch only ever touches local memory)
+    b0 = B - 1
     pages = indices[indptr[b0]:indptr[b0 + 1]]
-    kk = k[torch.from_numpy(pages.astype(np.int64)).to(dev)].reshape(-1, HKV, D)[:lens[b0]].float()
-    vv = v[torch.from_numpy(pages.astype(np.int64)).to(dev)].reshape(-1, HKV, D)[:lens[b0]].float()
-    qq = d_q[b0].float().view(HKV, HQ // HKV, D)
+    kk = k[torch.from_numpy(pages.astype(np.int64)).to(dev)].reshape(-1, hk, D)[:lens[b0]].float()
+    vv = v[torch.from_numpy(pages.astype(np.int64)).to(dev)].reshape(-1, hk, D)[:lens[b0]].float()
+    qq = d_q[b0].float().view(hk, HQ // HKV, D)
     s_ = torch.einsum("hgd,lhd->hgl", qq, kk) / math.sqrt(D)
-    ref = torch.einsum("hgl,lhd->hgd", torch.softmax(s_, -1), vv).reshape(HQ, D)
-    chk_err = float((out[b0].float() - ref).abs().max())
+    ref = torch.einsum("hgl,lhd->hgd", torch.softmax(s_, -1), vv).reshape(hq, D).cpu()
+    if world > 1:
+        import torch.distributed as dist
+        refs = [None] * world
+        dist.all_gather_object(refs, ref)
+        ref = torch.cat(refs)
+    chk_err = float((out[b0].float().cpu() - ref).abs().max()) if rank == 0 else 0.0
 
     peak, peak_kind = measured_peak()
     achieved = byts / (kern_ms * 1e-3) / 1e9
     extras = {}
-    if world == 1 and not args.no_extras:
+    if not args.no_extras:
         del k, v
         torch.cuda.empty_cache()
-        timer = ColdTimer(dev)
-        extras["config2_sweep"] = sweep_config2(ckl, dev, timer, peak)
-        extras["config3_cascade"] = bench_cascade(ckl, dev, timer, peak)
-        extras["config4_moe_w4a16_layer"] = bench_moe(ckl, dev, timer, peak)
-        extras["config5_mixtral_layer"] = bench_mixtral_layer(ckl, dev, timer, peak)
-        extras["extras_timing"] = "cold L2 (256 MB memset before each sample), median of 15"
+        timer = ColdTimer(dev, world)
+        if world == 1:
+            extras["config2_sweep"] = sweep_config2(ckl, dev, timer, peak)
+            extras["config3_cascade"] = bench_cascade(ckl, dev, timer, peak)
+            extras["config4_moe_w4a16_layer"] = bench_moe(ckl, dev, timer, peak)
+            extras["config5_mixtral_layer"] = bench_mixtral_layer(ckl, dev, timer, peak)
+        else:
+            ex = ckl.torch_exchange()
+            extras["config4_moe_w4a16_layer_ep"] = bench_moe_ep(ckl, dev, timer, peak, rank,
+                                                                world, ex)
+            extras["config5_mixtral_layer_tp_ep"] = bench_mixtral_ep(ckl, dev, timer, peak,
+                                                                     rank, world, ex)
+        extras["extras_timing"] = ("cold L2 (256 MB memset before each sample), median of 15"
+                                   + ("; ranks start each sample together (barrier), max over "
+                                      "ranks" if world > 1 else ""))
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline_sample(int(lens.max()), os.cpu_count() or 1)
@@ -688,9 +888,11 @@ def run_ours(args):
                          "frac": achieved / peak, "peak_source": peak_kind,
                          "kernel": "decode_partial_kernel<4>",
                          "algorithmic_bytes_per_launch": byts,
-                         "traffic": committed_traffic("decode_partial_kernel<4>", args.workload)},
+                         "traffic": committed_traffic("decode_partial_kernel<4>", args.workload)
+                                    if world == 1 else None},
             "e2e": {"value": byts * world / (e2e_ms * 1e-3) / 1e9, "unit": "GB/s",
-                    "ms_per_step": e2e_ms, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+                    "ms_per_step": e2e_ms, "h2d_bytes_per_step": h2d * world,
+                    "d2h_bytes_per_step": d2h},
             "gpu_launches": launches_per_step * args.steps,
             "plan": {"num_chunks": nc, "chunk_tokens": ct},
             "check_max_abs_err_vs_fp32": chk_err,
@@ -701,6 +903,9 @@ def run_ours(args):
         print(json.dumps(line))
     if world > 1:
         import torch.distributed as dist
+        torch.cuda.synchronize()
+        win.close()
+        grp.close()
         dist.barrier()
         dist.destroy_process_group()
     return 0
