@@ -9,16 +9,20 @@
 //   route     (1 CTA)    top-k, counts, offsets, stable slot order for this rank's tokens
 //   dispatch  (A CTAs)   writes the token row of assignment i into the owner's window, slab
 //                        `rank`, at position inv_perm[i] - offsets[first expert of owner]
-//                        (expert order within the slab), plus this rank's per-expert counts;
-//                        the last CTA raises the dispatch flag of every owner
-//   receive   (1 CTA)    waits for every source's flag, then builds the expert offsets and
-//                        the gather map (row -> slab position) over all received rows
+//                        (expert order within the slab), plus this rank's per-expert counts
+//   receive   (1 CTA)    raises this rank's dispatch flag in every owner's window, waits for
+//                        every source's flag, then builds the expert offsets and the gather
+//                        map (row -> slab position) over all received rows
 //   gate/up   GEMM       SwiGLU over the received rows (gathered through the map)
 //   down      GEMM       writes output row a to the window's y at the row's slab position
-//   signal    (1 CTA)    raises the ready flag of every source
-//   combine   (T CTAs)   waits for every owner's ready flag, reads its assignments' rows
-//                        from the owners' windows and sums them in fixed slot order
+//   combine   (T CTAs)   raises this rank's ready flag in every source's window, waits for
+//                        every owner's ready flag, reads its assignments' rows from the
+//                        owners' windows and sums them in fixed slot order
 //
+// A flag is raised by a release store at system scope from the kernel that follows the
+// writes it covers (stream order, griddepcontrol.wait), so the writes of the previous kernel
+// -- the dispatch's row stores into peer memory, the down GEMM's outputs -- are ordered
+// before it without a fence in every writing thread; a reader acquires the flag, then reads.
 // Flags carry epochs (calls completed on the rank, +1), so windows never need resetting.
 // One window per rank is enough: a source writes call i+1's rows only after its combine of
 // call i saw every owner's ready flag, i.e. after every owner finished reading call i's
@@ -48,8 +52,7 @@ constexpr int EP_MAX_E = 256;
 constexpr int EP_DISP_FLAG = 0;     // [CKL_EP_MAX_RANKS]: epoch of source s's last dispatch
 constexpr int EP_READY_FLAG = 64;   // [CKL_EP_MAX_RANKS]: epoch of owner o's last outputs
 constexpr int EP_EPOCH = 128;       // calls completed on this rank
-constexpr int EP_CNT_DISP = 132;    // dispatch CTAs finished (last-CTA detection)
-constexpr int EP_CNT_COMB = 136;    // combine CTAs finished
+constexpr int EP_CNT_COMB = 136;    // combine CTAs finished (last-CTA detection)
 constexpr int EP_CTRL_BYTES = 256;
 constexpr int RECV_THREADS = 512;
 
@@ -98,7 +101,6 @@ ep_dispatch_kernel(const EpArgs p, const __half* __restrict__ X, const int* __re
                    const int* __restrict__ counts, int A) {
     pdl_wait();                                       // routing results
     pdl_trigger();
-    const unsigned epoch = next_epoch(p);
     const int i = blockIdx.x;
     if (i < A) {
         const int e = __ldg(ids + i);
@@ -115,17 +117,6 @@ ep_dispatch_kernel(const EpArgs p, const __half* __restrict__ X, const int* __re
             reinterpret_cast<int*>(p.win[o] + p.off_counts)[p.rank * p.E_loc + (e - o * p.E_loc)] =
                 __ldg(counts + e);
         }
-    __threadfence_system();                           // this thread's peer stores first
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        unsigned* cnt = ctrl(p.win[p.rank], EP_CNT_DISP);
-        if (atomicAdd(cnt, 1u) == gridDim.x - 1) {    // last CTA: every row has been written
-            atomicExch(cnt, 0u);
-            __threadfence_system();
-            for (int o = 0; o < p.world; o++)
-                st_release_sys(ctrl(p.win[o], EP_DISP_FLAG) + p.rank, epoch);
-        }
-    }
 }
 
 // grid = 1: waits for every source, then the expert offsets over the received rows
@@ -137,12 +128,17 @@ ep_receive_kernel(const EpArgs p, int* __restrict__ offsets_loc, int* __restrict
     __shared__ int s_soff[EP_MAX_E];   // slab offset of (s, e)
     __shared__ int s_base[EP_MAX_E];   // first gathered row of (s, e)
     __shared__ int s_off[EP_MAX_E + 1];
-    pdl_wait();                                       // our own dispatch has completed
+    pdl_wait();                                       // our dispatch has completed
+    pdl_trigger();                                    // the gate/up GEMM waits for our results
     const unsigned epoch = next_epoch(p);
     uint8_t* own = p.win[p.rank];
-    if (threadIdx.x < p.world)
+    if (threadIdx.x < p.world) {
+        // our rows and counts are in every owner's window: raise our flag there, then wait
+        // for every source's flag here
+        st_release_sys(ctrl(p.win[threadIdx.x], EP_DISP_FLAG) + p.rank, epoch);
         wait_epoch(ctrl(own, EP_DISP_FLAG) + threadIdx.x, epoch,
                    globaltimer() + p.timeout_ns, p.err);
+    }
     __syncthreads();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
     const int nse = p.world * p.E_loc;
@@ -204,30 +200,22 @@ ep_receive_kernel(const EpArgs p, int* __restrict__ offsets_loc, int* __restrict
     }
 }
 
-// grid = 1, 32 threads: after the down GEMM, raise every source's ready flag.
-__global__ void ep_signal_kernel(const EpArgs p) {
-    pdl_wait();                                       // expert outputs written
-    pdl_trigger();
-    const unsigned epoch = next_epoch(p);
-    if ((int)threadIdx.x < p.world) {
-        __threadfence_system();
-        st_release_sys(ctrl(p.win[threadIdx.x], EP_READY_FLAG) + p.rank, epoch);
-    }
-}
-
-// grid = max(T, 1), 256 threads: out[t] = sum_{j<k} wts[t][j] * y_owner[slab row] in fixed j
-// order with fp32 accumulation (the arithmetic of the single-GPU combine); the last CTA
-// advances the rank's epoch.
+// grid = max(T, 1), 256 threads: every CTA raises this rank's ready flag in every source's
+// window (the down GEMM's outputs are complete), waits for every owner's, then
+// out[t] = sum_{j<k} wts[t][j] * y_owner[slab row] in fixed j order with fp32 accumulation
+// (the arithmetic of the single-GPU combine); the last CTA advances the rank's epoch.
 __global__ void __launch_bounds__(256)
 ep_combine_kernel(const EpArgs p, const int* __restrict__ ids, const int* __restrict__ inv_perm,
                   const int* __restrict__ offsets, const float* __restrict__ wts,
                   __half* __restrict__ out, int T) {
-    pdl_wait();
+    pdl_wait();                                       // the down GEMM has completed
     const unsigned epoch = next_epoch(p);
     uint8_t* own = p.win[p.rank];
-    if ((int)threadIdx.x < p.world)
+    if ((int)threadIdx.x < p.world) {
+        st_release_sys(ctrl(p.win[threadIdx.x], EP_READY_FLAG) + p.rank, epoch);
         wait_epoch(ctrl(own, EP_READY_FLAG) + threadIdx.x, epoch,
                    globaltimer() + p.timeout_ns, p.err);
+    }
     __syncthreads();
     const int t = blockIdx.x;
     if (t < T) {
@@ -445,11 +433,6 @@ ckl_status ckl_moe_ep_layer(const ckl_moe_ep_comm* comm, const float* logits, co
     st = expert_gemm(h, nullptr, offsets_loc, L.A_max, comm->T_cap * comm->world, down, nullptr,
                      own + L.y, 1, 0, split, split_bytes, stream, s2 > 0 ? 1 : 2, row_src, a_rows);
     if (st != CKL_OK) return st;
-    {
-        void* args[] = {&p};
-        CKL_CUDA_TRY(launch(reinterpret_cast<const void*>(ep_signal_kernel), dim3(1), dim3(32), 0, s,
-                            args, true));
-    }
     {
         __half* o16 = static_cast<__half*>(out);
         void* args[] = {&p, &ids, &inv_perm, &offsets, &wts, &o16, &T};
