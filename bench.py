@@ -552,6 +552,55 @@ def bench_mixtral_layer(ckl, dev, timer, peak):
     return res
 
 
+def bench_grouped_gemm(ckl, dev, timer, peak):
+    """The dense grouped expert GEMM (ckl_moe_grouped_gemm, tcgen05) on the reference's
+    performance shapes (02_moe_grouped_gemm.cu:342-344): routed and permuted once, then the
+    GEMM alone with a cold L2. Bound: HBM (every shape streams more weight bytes than the
+    tensor cores need time for); both fractions are reported. Beside it, for context, the
+    reference's baseline (a): one cuBLAS GEMM per expert through torch.matmul."""
+    import torch
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as fh:
+            tf_peak = float(json.load(fh)["bf16_tflops"])
+    except (OSError, KeyError, ValueError):
+        tf_peak = 1590.0
+    res = {}
+    for name, (T, E, k, d, f) in {"mixtral_prefill_T512": (512, 8, 2, 4096, 14336),
+                                  "finegrained_prefill_T512": (512, 64, 6, 2048, 1408),
+                                  "finegrained_decode_T16": (16, 64, 6, 2048, 1408)}.items():
+        g = torch.Generator(device=dev)
+        g.manual_seed(T + E)
+        lg = torch.randn((T, E), generator=g, device=dev)
+        X = (torch.rand((T, d), generator=g, device=dev) * 2 - 1).half()
+        W = ((torch.rand((E, d, f), generator=g, device=dev) * 2 - 1) / d ** 0.5).half()
+        r = ckl.route_and_permute(lg, X, k)
+        Xp, off = r["Xp"], r["offsets"]
+        Yp = torch.empty((T * k, f), dtype=torch.float16, device=dev)
+        offs = off.cpu().numpy().tolist()
+        active = sum(1 for e in range(E) if offs[e + 1] > offs[e])
+        A = T * k
+        byts = active * d * f * 2 + A * d * 2 + A * f * 2
+        flops = 2.0 * A * d * f
+        t = timer(lambda: ckl.grouped_gemm(Xp, W, off, out=Yp))
+
+        def per_expert():
+            for e in range(E):
+                if offs[e + 1] > offs[e]:
+                    torch.matmul(Xp[offs[e]:offs[e + 1]], W[e], out=Yp[offs[e]:offs[e + 1]])
+        t_ref = timer(per_expert)
+        res[name] = {"us": round(t * 1e3, 1), "active_experts": active,
+                     "tokens_per_expert": round(A / E, 1),
+                     "GB/s": round(byts / (t * 1e-3) / 1e9, 1),
+                     "frac_of_measured_hbm": round(byts / (t * 1e-3) / 1e9 / peak, 3),
+                     "TFLOP/s": round(flops / (t * 1e-3) / 1e12, 1),
+                     "frac_of_measured_bf16_tensor": round(flops / (t * 1e-3) / 1e12 / tf_peak, 3),
+                     "us_cublas_per_expert_loop": round(t_ref * 1e3, 1)}
+        del W, Xp, Yp, r
+        torch.cuda.empty_cache()
+    res["method"] = "cold L2 (256 MB memset before each sample), median of 15; bytes = active experts' fp16 weights + Xp + Yp"
+    return res
+
+
 def _split(T, world, rank):
     return T // world + (1 if rank < T % world else 0)
 
@@ -864,6 +913,7 @@ def run_ours(args):
             extras["config3_cascade"] = bench_cascade(ckl, dev, timer, peak)
             extras["config4_moe_w4a16_layer"] = bench_moe(ckl, dev, timer, peak)
             extras["config5_mixtral_layer"] = bench_mixtral_layer(ckl, dev, timer, peak)
+            extras["grouped_gemm_tcgen05"] = bench_grouped_gemm(ckl, dev, timer, peak)
         else:
             ex = ckl.torch_exchange()
             extras["config4_moe_w4a16_layer_ep"] = bench_moe_ep(ckl, dev, timer, peak, rank,

@@ -123,6 +123,8 @@ _SIGS = {
                                         C.c_void_p, C.c_void_p]),
     "ckl_moe_combine": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p,
                                   C.c_int, C.c_int, C.c_int, C.c_void_p]),
+    "ckl_moe_grouped_gemm": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int,
+                                       C.c_int, C.c_int, C.c_int, C.c_void_p]),
     "ckl_moe_layer_workspace_size": (C.c_size_t, [C.c_int, C.c_int, C.POINTER(MoeWeights),
                                                   C.POINTER(MoeWeights)]),
     "ckl_moe_layer": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_int,
@@ -453,6 +455,21 @@ def expert_gemm_ex(X, row_src, offsets, A, gate, up=None, y_f32=False, force_ksp
                                        force_ksplit, _ptr(ws), need, _stream(stream)),
           "ckl_moe_expert_gemm_ex")
     return Y
+
+
+def grouped_gemm(Xp, W, offsets, out=None, stream=None):
+    """moe_grouped_gemm (02_moe_grouped_gemm.cu:86-186): Yp[r] = Xp[r] . W[e] over the
+    expert-sorted rows, fp16 [A][f] (tcgen05). W fp16 [E][d][f]."""
+    torch = _torch()
+    _need(Xp, torch.float16, "Xp")
+    _need(W, torch.float16, "W")
+    A, d = Xp.shape
+    E, _, f = W.shape
+    if out is None:
+        out = torch.empty((A, f), dtype=torch.float16, device=Xp.device)
+    check(lib().ckl_moe_grouped_gemm(_ptr(Xp), _ptr(W), _ptr(out), _ptr(offsets), A, E, d, f,
+                                     _stream(stream)), "ckl_moe_grouped_gemm")
+    return out
 
 
 def route_and_permute(logits, X, k, bm=0, permute=True, stream=None):

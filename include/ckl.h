@@ -274,6 +274,15 @@ CKL_API ckl_status ckl_moe_combine(const void* Yp, int y_f32, const int* inv_per
                                    const float* wts, void* out, int T, int k, int f,
                                    void* stream);
 
+/* moe_grouped_gemm (02_moe_grouped_gemm.cu:86-186), the dense path for batches with tens of
+ * tokens or more per expert: Yp[r] = Xp[r] . W[e] for the rows r in [offsets[e],
+ * offsets[e+1]) of every expert, fp16 in, fp32 accumulation, fp16 out. Xp [A][d] sorted by
+ * expert (ckl_moe_route_permute), W fp16 [E][d][f] row-major (the reference's layout),
+ * offsets [E+1] device. tcgen05 tensor cores, one launch, device-side schedule (no host
+ * sync). d % 64 == 0, f % 128 == 0. */
+CKL_API ckl_status ckl_moe_grouped_gemm(const void* Xp, const void* W, void* Yp, const int* offsets,
+                                        int A, int E, int d, int f, void* stream);
+
 /* Workspace of ckl_moe_layer. */
 CKL_API size_t ckl_moe_layer_workspace_size(int T, int k, const ckl_moe_weights* gate,
                                             const ckl_moe_weights* down);
