@@ -357,7 +357,8 @@ def paged_batch(lens, dev, seed, Lp=0):
 
 
 def sweep_config2(ckl, dev, timer, peak):
-    """Every config-2 shape through ckl_decode_attention, cold L2, median of 15."""
+    """Every config-2 shape through ckl_decode_attention (the reference's chunked split) and
+    ckl_decode_attention_balanced, cold L2, median of 15."""
     import torch
     rows = {}
     for name in ("1x32768", "8x8192", "64x1024", "256x4096", "ragged256"):
@@ -373,7 +374,15 @@ def sweep_config2(ckl, dev, timer, peak):
         gbs = algorithmic_bytes(lens) / (ms * 1e-3) / 1e9
         rows[name] = {"ms": round(ms, 4), "GB/s": round(gbs, 1),
                       "frac_of_measured_hbm": round(gbs / peak, 3), "chunks": nc}
-        del d, out, lse, ws
+        # the balanced split (ckl_decode_attention_balanced), the path for ragged batches
+        pb = ckl.make_params(**d, num_chunks=1, chunk_tokens=16)
+        wsb = torch.empty(max(ckl.lib().ckl_decode_balanced_workspace_size(ckl.C.byref(pb)), 256),
+                          dtype=torch.uint8, device=dev)
+        msb = timer(lambda: ckl.decode_attention_balanced(**d, out=out, lse=lse, workspace=wsb))
+        gbb = algorithmic_bytes(lens) / (msb * 1e-3) / 1e9
+        rows[name]["balanced_split"] = {"ms": round(msb, 4), "GB/s": round(gbb, 1),
+                                        "frac_of_measured_hbm": round(gbb / peak, 3)}
+        del d, out, lse, ws, wsb
         torch.cuda.empty_cache()
     return rows
 

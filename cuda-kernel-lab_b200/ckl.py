@@ -90,6 +90,9 @@ _SIGS = {
                                    C.c_int, C.c_void_p]),
     "ckl_decode_attention": (C.c_int, [C.POINTER(DecodeParams), C.c_void_p, C.c_void_p,
                                        C.c_void_p, C.c_size_t, C.c_void_p]),
+    "ckl_decode_balanced_workspace_size": (C.c_size_t, [C.POINTER(DecodeParams)]),
+    "ckl_decode_attention_balanced": (C.c_int, [C.POINTER(DecodeParams), C.c_void_p, C.c_void_p,
+                                                C.c_void_p, C.c_size_t, C.c_void_p]),
     "ckl_decode_attention_noalloc": (C.c_int, [C.POINTER(DecodeParams), C.c_void_p,
                                                C.c_void_p, C.c_void_p]),
     "ckl_validate_page_table": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int,
@@ -304,6 +307,26 @@ def decode_attention(q, k_cache, v_cache, kv_indptr, kv_indices, kv_last_page_le
     ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
     check(lib().ckl_decode_attention(C.byref(p), _ptr(out), _ptr(lse), _ptr(workspace),
                                      ws_bytes, _stream(stream)), "ckl_decode_attention")
+    return out, lse
+
+
+def decode_attention_balanced(q, k_cache, v_cache, kv_indptr, kv_indices, kv_last_page_len, *,
+                              out=None, lse=None, workspace=None, sm_scale=None, stream=None):
+    """The balanced split (ckl_decode_attention_balanced): returns (out, lse)."""
+    torch = _torch()
+    B, Hq, _ = q.shape
+    p = make_params(q, k_cache, v_cache, kv_indptr, kv_indices, kv_last_page_len, num_chunks=1,
+                    chunk_tokens=16, sm_scale=sm_scale)
+    if out is None:
+        out = torch.empty_like(q)
+    if lse is None:
+        lse = torch.empty((B, Hq), dtype=torch.float32, device=q.device)
+    need = lib().ckl_decode_balanced_workspace_size(C.byref(p))
+    if workspace is None or workspace.numel() * workspace.element_size() < need:
+        workspace = torch.empty(max(need, 256), dtype=torch.uint8, device=q.device)
+    check(lib().ckl_decode_attention_balanced(C.byref(p), _ptr(out), _ptr(lse), _ptr(workspace),
+                                              workspace.numel() * workspace.element_size(),
+                                              _stream(stream)), "ckl_decode_attention_balanced")
     return out, lse
 
 

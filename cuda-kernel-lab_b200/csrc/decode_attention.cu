@@ -93,8 +93,7 @@ decode_partial_kernel(const __grid_constant__ CUtensorMap tmK,
     const uint64_t deadline = globaltimer() + a.timeout_ns;
 
     // consumer state (unused by the producer warp)
-    float o[16][4];
-    float m_lo = -INFINITY, m_hi = -INFINITY, l_lo = 0.f, l_hi = 0.f;
+    HeadState<G> hs;
     const int g = lane >> 2, t = lane & 3;
 
     if (warp == CONSUMERS) {
@@ -132,131 +131,25 @@ decode_partial_kernel(const __grid_constant__ CUtensorMap tmK,
         }
     } else {
         // ---------------------------------------------------------------- consumer warps
-        // q fragments (A operand: rows = the G query heads of this kv head, cols = dims)
-        uint32_t qa0[8], qa1[8], qa2[8], qa3[8];
-#pragma unroll
-        for (int kk = 0; kk < 8; kk++) qa0[kk] = qa1[kk] = qa2[kk] = qa3[kk] = 0u;
-        if (g < G) {
-            const uint32_t* qrow = reinterpret_cast<const uint32_t*>(
-                a.q + ((size_t)b * a.Hq + (size_t)kvh * G + g) * D);
-#pragma unroll
-            for (int kk = 0; kk < 8; kk++) {
-                qa0[kk] = __ldg(qrow + 8 * kk + t);
-                qa2[kk] = __ldg(qrow + 8 * kk + 4 + t);
-            }
-            if (HI) {
-                const uint32_t* qhi = qrow + 8 * D / 2;
-#pragma unroll
-                for (int kk = 0; kk < 8; kk++) {
-                    qa1[kk] = __ldg(qhi + 8 * kk + t);
-                    qa3[kk] = __ldg(qhi + 8 * kk + 4 + t);
-                }
-            }
-        }
-#pragma unroll
-        for (int j = 0; j < 16; j++) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
-
-        // ldmatrix lane addressing (see tile_off): K as the B operand of Q K^T, non-trans:
-        // lanes 0-7 keys 0-7 / dims 16kk..+7, 8-15 keys 0-7 / +8..15, 16-31 keys 8-15.
-        const int k_key = (lane & 7) + ((lane >> 4) << 3), k_hi = (lane >> 3) & 1;
-        // V as the B operand of P V, transposed: lanes 0-7 keys 0-7, 8-15 keys 8-15 of dim
-        // chunk 2jj, lanes 16-31 the same for chunk 2jj+1.
-        const int v_key = (lane & 7) + (((lane >> 3) & 1) << 3), v_hi = lane >> 4;
-
+        hs.load_q(a.q + ((size_t)b * a.Hq + (size_t)kvh * G) * D, lane);
+        hs.reset();
         bool ok = true;
         for (int i = warp; i < npg; i += CONSUMERS) {
             const int s = i % STAGES;
             const bool got = mbar_wait(&full[s], (i / STAGES) & 1, deadline, a.err);
             if (!__all_sync(0xffffffffu, got)) { ok = false; break; }
-            const uint32_t kb = smem_u32(ring + s * STAGE_BYTES);
-            const uint32_t vb = kb + KV_TILE;
-
-            float sc[2][4];
-#pragma unroll
-            for (int n = 0; n < 2; n++) sc[n][0] = sc[n][1] = sc[n][2] = sc[n][3] = 0.f;
-#pragma unroll
-            for (int kk = 0; kk < 8; kk++) {
-                uint32_t b00, b01, b10, b11;
-                ldmatrix_x4(kb + tile_off(k_key, 2 * kk + k_hi), b00, b01, b10, b11);
-                mma_16816(sc[0], qa0[kk], qa1[kk], qa2[kk], qa3[kk], b00, b01);
-                mma_16816(sc[1], qa0[kk], qa1[kk], qa2[kk], qa3[kk], b10, b11);
-            }
-            // mask keys past the chunk end (only the sequence's last page is partial)
-            const int kbase = (p0 + i) * PAGE;
-            if (kbase + PAGE > kend) {
-#pragma unroll
-                for (int n = 0; n < 2; n++)
-#pragma unroll
-                    for (int c = 0; c < 4; c++)
-                        if (kbase + n * 8 + 2 * t + (c & 1) >= kend) sc[n][c] = -INFINITY;
-            }
-#pragma unroll
-            for (int n = 0; n < 2; n++)
-#pragma unroll
-                for (int c = 0; c < 4; c++) sc[n][c] *= a.scale_log2;
-
-            float mx_lo = fmaxf(fmaxf(sc[0][0], sc[0][1]), fmaxf(sc[1][0], sc[1][1]));
-            mx_lo = fmaxf(mx_lo, __shfl_xor_sync(0xffffffffu, mx_lo, 1));
-            mx_lo = fmaxf(mx_lo, __shfl_xor_sync(0xffffffffu, mx_lo, 2));
-            float mx_hi = -INFINITY;
-            if (HI) {
-                mx_hi = fmaxf(fmaxf(sc[0][2], sc[0][3]), fmaxf(sc[1][2], sc[1][3]));
-                mx_hi = fmaxf(mx_hi, __shfl_xor_sync(0xffffffffu, mx_hi, 1));
-                mx_hi = fmaxf(mx_hi, __shfl_xor_sync(0xffffffffu, mx_hi, 2));
-            }
-            const bool need = mx_lo > m_lo + RESCALE_THRESHOLD || (HI && mx_hi > m_hi + RESCALE_THRESHOLD);
-            if (__any_sync(0xffffffffu, need)) {
-                const float mn_lo = fmaxf(m_lo, mx_lo);
-                const float c_lo = ex2(m_lo - mn_lo);
-                m_lo = mn_lo;
-                l_lo *= c_lo;
-#pragma unroll
-                for (int j = 0; j < 16; j++) { o[j][0] *= c_lo; o[j][1] *= c_lo; }
-                if (HI) {
-                    const float mn_hi = fmaxf(m_hi, mx_hi);
-                    const float c_hi = ex2(m_hi - mn_hi);
-                    m_hi = mn_hi;
-                    l_hi *= c_hi;
-#pragma unroll
-                    for (int j = 0; j < 16; j++) { o[j][2] *= c_hi; o[j][3] *= c_hi; }
-                }
-            }
-            const float p00 = ex2(sc[0][0] - m_lo), p01 = ex2(sc[0][1] - m_lo);
-            const float p10 = ex2(sc[1][0] - m_lo), p11 = ex2(sc[1][1] - m_lo);
-            l_lo += (p00 + p01) + (p10 + p11);
-            const uint32_t pa0 = pack_half2(p00, p01), pa2 = pack_half2(p10, p11);
-            uint32_t pa1 = 0u, pa3 = 0u;
-            if (HI) {
-                const float q00 = ex2(sc[0][2] - m_hi), q01 = ex2(sc[0][3] - m_hi);
-                const float q10 = ex2(sc[1][2] - m_hi), q11 = ex2(sc[1][3] - m_hi);
-                l_hi += (q00 + q01) + (q10 + q11);
-                pa1 = pack_half2(q00, q01);
-                pa3 = pack_half2(q10, q11);
-            }
-#pragma unroll
-            for (int jj = 0; jj < 8; jj++) {
-                uint32_t v0, v1, v2, v3;
-                ldmatrix_x4_trans(vb + tile_off(v_key, 2 * jj + v_hi), v0, v1, v2, v3);
-                mma_16816(o[2 * jj], pa0, pa1, pa2, pa3, v0, v1);
-                mma_16816(o[2 * jj + 1], pa0, pa1, pa2, pa3, v2, v3);
-            }
+            hs.page(smem_u32(ring + s * STAGE_BYTES), (p0 + i) * PAGE, kend, a.scale_log2, lane);
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[s]);
         }
-
-        l_lo += __shfl_xor_sync(0xffffffffu, l_lo, 1);
-        l_lo += __shfl_xor_sync(0xffffffffu, l_lo, 2);
-        if (HI) {
-            l_hi += __shfl_xor_sync(0xffffffffu, l_hi, 1);
-            l_hi += __shfl_xor_sync(0xffffffffu, l_hi, 2);
-        }
-        if (!ok) { m_lo = m_hi = -INFINITY; l_lo = l_hi = 0.f; }
+        hs.reduce_l();
+        if (!ok) { hs.m_lo = hs.m_hi = -INFINITY; hs.l_lo = hs.l_hi = 0.f; }
         if (t == 0) {
-            m_red[warp * 16 + g] = m_lo;
-            l_red[warp * 16 + g] = l_lo;
+            m_red[warp * 16 + g] = hs.m_lo;
+            l_red[warp * 16 + g] = hs.l_lo;
             if (HI) {
-                m_red[warp * 16 + g + 8] = m_hi;
-                l_red[warp * 16 + g + 8] = l_hi;
+                m_red[warp * 16 + g + 8] = hs.m_hi;
+                l_red[warp * 16 + g + 8] = hs.l_hi;
             }
         }
     }
@@ -269,16 +162,16 @@ decode_partial_kernel(const __grid_constant__ CUtensorMap tmK,
 #pragma unroll
             for (int j = 0; j < 16; j++) {
                 float* dst = ost + ((size_t)warp * G + g) * D + 8 * j + 2 * t;
-                dst[0] = o[j][0];
-                dst[1] = o[j][1];
+                dst[0] = hs.o[j][0];
+                dst[1] = hs.o[j][1];
             }
         }
         if (HI && g + 8 < G) {
 #pragma unroll
             for (int j = 0; j < 16; j++) {
                 float* dst = ost + ((size_t)warp * G + g + 8) * D + 8 * j + 2 * t;
-                dst[0] = o[j][2];
-                dst[1] = o[j][3];
+                dst[0] = hs.o[j][2];
+                dst[1] = hs.o[j][3];
             }
         }
     }

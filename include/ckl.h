@@ -121,6 +121,19 @@ CKL_API ckl_status ckl_merge_states(const float* part_o, const float* part_lse, 
 CKL_API ckl_status ckl_decode_attention(const ckl_decode_params* p, void* out, float* lse,
                                 void* workspace, size_t workspace_bytes, void* stream);
 
+/* Balanced split (no reference counterpart: the reference lists it as not done,
+ * README.md:54). The pages of all (sequence, kv head) units are divided exactly evenly over
+ * one wave of persistent CTAs (SMs x resident CTAs per SM), with a partial wherever a CTA's
+ * run of pages crosses a unit boundary and an LSE merge after -- no idle tail wave and one
+ * pipeline ramp per CTA. Computed on the device from the page table (no host plan).
+ * Requires kv_start == 0; num_chunks / chunk_tokens / chunk_base / part_stride / part_o /
+ * part_lse are ignored. Same results as ckl_decode_attention up to the fp32 summation
+ * order of the split. */
+CKL_API size_t ckl_decode_balanced_workspace_size(const ckl_decode_params* p);
+CKL_API ckl_status ckl_decode_attention_balanced(const ckl_decode_params* p, void* out, float* lse,
+                                                 void* workspace, size_t workspace_bytes,
+                                                 void* stream);
+
 /* Size of the scratch built into the library for ckl_decode_attention_noalloc. */
 #define CKL_NOALLOC_SCRATCH_BYTES (16u << 20)
 
