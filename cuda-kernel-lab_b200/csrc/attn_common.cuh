@@ -193,7 +193,7 @@ ckl_status validate(const ckl_decode_params* p, int* G);
 // (out_heads 0 = Hq).
 ckl_status launch_partial(const ckl_decode_params* p, int G, bool direct, __half* out,
                           float* lse, float* part_o, float* part_lse, cudaStream_t stream,
-                          int out_heads = 0, int head_offset = 0);
+                          int out_heads = 0, int head_offset = 0, bool pdl = false);
 size_t part_o_bytes(const ckl_decode_params* p);
 
 }  // namespace attn

@@ -70,6 +70,7 @@ cascade_prefix_kernel(const __grid_constant__ CUtensorMap tmK,
     }
     __syncthreads();
     const uint64_t deadline = globaltimer() + a.timeout_ns;
+    pdl_trigger();                   // the suffix kernel (independent slots) may start now
 
     if (warp == PWARPS) {
         // ---------------------------------------------------------------- producer warp
@@ -412,7 +413,10 @@ ckl_status ckl_cascade_decode(const ckl_cascade_plan_t* plan, void* out, float* 
                                                attn::part_o_bytes(&plan->suffix));
     st = launch_prefix(plan, part_o, part_lse, s);
     if (st != CKL_OK) return st;
-    st = attn::launch_partial(&plan->suffix, G, false, nullptr, nullptr, part_o, part_lse, s);
+    // the suffix writes other slots than the prefix: it runs alongside it (programmatic
+    // dependent launch) and only its completion waits for the prefix; the merge waits for both
+    st = attn::launch_partial(&plan->suffix, G, false, nullptr, nullptr, part_o, part_lse, s, 0, 0,
+                              true);
     if (st != CKL_OK) return st;
     return ckl_merge_states(part_o, part_lse, out, lse, plan->suffix.B * plan->suffix.Hq,
                             plan->suffix.part_stride, stream);

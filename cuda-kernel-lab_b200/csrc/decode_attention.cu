@@ -91,6 +91,7 @@ decode_partial_kernel(const __grid_constant__ CUtensorMap tmK,
     }
     __syncthreads();
     const uint64_t deadline = globaltimer() + a.timeout_ns;
+    pdl_trigger();                   // a merge launched after us may be scheduled now
 
     // consumer state (unused by the producer warp)
     HeadState<G> hs;
@@ -207,6 +208,9 @@ decode_partial_kernel(const __grid_constant__ CUtensorMap tmK,
             if (d == 0) a.part_lse[slot] = lse_v;
         }
     }
+    // launched dependent on another kernel (the cascade's suffix after its prefix): do not
+    // complete before it, so that a kernel waiting on us has both kernels' partials
+    pdl_wait();
 }
 
 // LSE merge: one warp per (sequence, q head) row, 4 dims per lane (16-byte loads). Row
@@ -217,6 +221,7 @@ __global__ void __launch_bounds__(256)
 merge_states_kernel(const float* __restrict__ part_o, const float* __restrict__ part_lse,
                     __half* __restrict__ out, float* __restrict__ lse_out, int rows, int slots,
                     int Hq, int out_heads, int head_offset) {
+    pdl_wait();                      // partials of the kernel(s) before us
     const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (row >= rows) return;
     const size_t orow = (size_t)(row / Hq) * out_heads + head_offset + row % Hq;
@@ -316,7 +321,7 @@ ckl_status validate(const ckl_decode_params* p, int* G) {
 
 ckl_status launch_partial(const ckl_decode_params* p, int G, bool direct, __half* out,
                           float* lse, float* part_o, float* part_lse, cudaStream_t stream,
-                          int out_heads, int head_offset) {
+                          int out_heads, int head_offset, bool pdl) {
     const DeviceInfo* di = device_info();
     if (!di) return CKL_CUDA_ERROR;
     const KernelSetup* ks = setup(di);
@@ -351,7 +356,7 @@ ckl_status launch_partial(const ckl_decode_params* p, int G, bool direct, __half
 
     void* args[] = {&tmK, &tmV, &a};
     dim3 grid((unsigned)(p->B * p->Hkv), (unsigned)p->num_chunks);
-    CKL_CUDA_TRY(cudaLaunchKernel(pick(G), grid, dim3(THREADS), args, SMEM_BYTES, stream));
+    CKL_CUDA_TRY(launch(pick(G), grid, dim3(THREADS), SMEM_BYTES, stream, args, pdl));
     return CKL_OK;
 }
 
@@ -419,9 +424,11 @@ ckl_status ckl_merge_states(const float* part_o, const float* part_lse, void* ou
     if (!part_o || !part_lse || !out || !lse) return fail(CKL_INVALID_ARG, "merge_states: NULL");
     if (((uintptr_t)part_o & 15) || ((uintptr_t)out & 7))
         return fail(CKL_INVALID_ARG, "merge_states: part_o 16-byte / out 8-byte alignment");
-    merge_states_kernel<<<ceil_div(rows, 8), 256, 0, (cudaStream_t)stream>>>(
-        part_o, part_lse, static_cast<__half*>(out), lse, rows, num_slots, 1, 1, 0);
-    CKL_CUDA_TRY(cudaGetLastError());
+    int rows_v = rows, slots_v = num_slots, one = 1, zero = 0;
+    __half* out_h = static_cast<__half*>(out);
+    void* args[] = {&part_o, &part_lse, &out_h, &lse, &rows_v, &slots_v, &one, &one, &zero};
+    CKL_CUDA_TRY(launch(reinterpret_cast<const void*>(merge_states_kernel), dim3(ceil_div(rows, 8)),
+                        dim3(256), 0, (cudaStream_t)stream, args, true));
     return CKL_OK;
 }
 
@@ -451,12 +458,11 @@ ckl_status decode_attention_rows(const ckl_decode_params* p, void* out, float* l
     float* part_lse = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + part_o_bytes(p));
     st = launch_partial(p, G, false, nullptr, nullptr, part_o, part_lse, s, 0, 0);
     if (st != CKL_OK) return st;
-    const int rows = p->B * p->Hq;
-    merge_states_kernel<<<ceil_div(rows, 8), 256, 0, s>>>(part_o, part_lse,
-                                                          static_cast<__half*>(out), lse, rows,
-                                                          p->part_stride, p->Hq, out_heads,
-                                                          head_offset);
-    CKL_CUDA_TRY(cudaGetLastError());
+    int rows = p->B * p->Hq, slots = p->part_stride, Hq = p->Hq;
+    __half* out_h = static_cast<__half*>(out);
+    void* args[] = {&part_o, &part_lse, &out_h, &lse, &rows, &slots, &Hq, &out_heads, &head_offset};
+    CKL_CUDA_TRY(launch(reinterpret_cast<const void*>(merge_states_kernel), dim3(ceil_div(rows, 8)),
+                        dim3(256), 0, s, args, true));
     return CKL_OK;
 }
 
