@@ -128,6 +128,9 @@ _SIGS = {
                                   C.c_int, C.c_int, C.c_int, C.c_void_p]),
     "ckl_moe_grouped_gemm": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int,
                                        C.c_int, C.c_int, C.c_int, C.c_void_p]),
+    "ckl_moe_weights_save": (C.c_int, [C.c_char_p, C.POINTER(MoeWeights), C.c_void_p]),
+    "ckl_moe_weights_file_info": (C.c_int, [C.c_char_p, C.POINTER(MoeWeights)]),
+    "ckl_moe_weights_load": (C.c_int, [C.c_char_p, C.POINTER(MoeWeights), C.c_void_p]),
     "ckl_moe_layer_workspace_size": (C.c_size_t, [C.c_int, C.c_int, C.POINTER(MoeWeights),
                                                   C.POINTER(MoeWeights)]),
     "ckl_moe_layer": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_int,
@@ -441,6 +444,36 @@ class QuantWeights:
         check(lib().ckl_moe_dequant_weights(C.byref(self.w), _ptr(out), _stream(stream)),
               "ckl_moe_dequant_weights")
         return out
+
+    def save(self, path, stream=None):
+        """Writes the packed weights to `path` (ckl_moe_weights_save)."""
+        check(lib().ckl_moe_weights_save(os.fsencode(path), C.byref(self.w), _stream(stream)),
+              "ckl_moe_weights_save")
+
+    @classmethod
+    def load(cls, path, device="cuda", stream=None):
+        """Packed weights read back from `path` (ckl_moe_weights_file_info + _load)."""
+        torch = _torch()
+        info = MoeWeights()
+        check(lib().ckl_moe_weights_file_info(os.fsencode(path), C.byref(info)),
+              "ckl_moe_weights_file_info")
+        self = cls.__new__(cls)
+        self.bits, self.E, self.K, self.N = info.bits, info.E, info.K, info.N
+        self.group, self.asym = info.group, bool(info.asym)
+        L = lib()
+        self.packed = torch.empty(L.ckl_moe_packed_bytes(info.bits, info.E, info.K, info.N, info.group),
+                                  dtype=torch.uint8, device=device)
+        ns = L.ckl_moe_scale_count(info.E, info.K, info.N, info.group) if info.bits != 16 else 1
+        self.scales = torch.empty(max(ns, 1), dtype=torch.float16, device=device)
+        nz = L.ckl_moe_zero_words(info.E, info.K, info.N, info.group) if info.asym else 1
+        self.zeros = torch.zeros(max(nz, 1), dtype=torch.int32, device=device)
+        self.w = MoeWeights(info.bits, info.E, info.K, info.N, info.group, info.asym,
+                            self.packed.data_ptr(),
+                            self.scales.data_ptr() if info.bits != 16 else None,
+                            self.zeros.data_ptr() if info.asym else None)
+        check(L.ckl_moe_weights_load(os.fsencode(path), C.byref(self.w), _stream(stream)),
+              "ckl_moe_weights_load")
+        return self
 
     def bytes_per_expert(self):
         """Algorithmic bytes of one expert: codes + scales (+ zero points)."""

@@ -296,6 +296,18 @@ CKL_API ckl_status ckl_moe_combine(const void* Yp, int y_f32, const int* inv_per
 CKL_API ckl_status ckl_moe_grouped_gemm(const void* Xp, const void* W, void* Yp, const int* offsets,
                                         int A, int E, int d, int f, void* stream);
 
+/* Stable on-disk format of packed expert weights (no reference counterpart: the reference
+ * quantises at start-up, 03_moe_wq_decode.cu:286-299). A 64-byte little-endian header
+ * (magic "CKLMOEW1", version 1, bits, E, K, N, group, asym, CRC-32 of the payload, the
+ * three section sizes; layout in csrc/moe_io.cu) followed by the packed codes, scales and
+ * zero points exactly as in device memory. save: device -> file; file_info: the header's
+ * shape into *w (buffer pointers set to NULL) so the caller can size the buffers
+ * (ckl_moe_packed_bytes ...); load: file -> the caller's device buffers, after checking
+ * the shape against *w and the checksum. Host functions: they synchronise `stream`. */
+CKL_API ckl_status ckl_moe_weights_save(const char* path, const ckl_moe_weights* w, void* stream);
+CKL_API ckl_status ckl_moe_weights_file_info(const char* path, ckl_moe_weights* w);
+CKL_API ckl_status ckl_moe_weights_load(const char* path, ckl_moe_weights* w, void* stream);
+
 /* Workspace of ckl_moe_layer. */
 CKL_API size_t ckl_moe_layer_workspace_size(int T, int k, const ckl_moe_weights* gate,
                                             const ckl_moe_weights* down);

@@ -84,3 +84,39 @@ def test_no_fallback_when_library_missing(tmp_path, monkeypatch):
     with pytest.raises(m.CklError):
         m.lib()
     # monkeypatch restores the loaded library (and its bound signatures) afterwards
+
+
+def _weights_header(bits=4, E=2, K=256, N=128, group=128, asym=1, crc=0, magic=b"CKLMOEW1",
+                    version=1, sizes=None):
+    import struct
+    import ckl
+    L = ckl.lib()
+    p = L.ckl_moe_packed_bytes(bits, E, K, N, group)
+    s = L.ckl_moe_scale_count(E, K, N, group) if bits != 16 else 0
+    z = L.ckl_moe_zero_words(E, K, N, group) if asym else 0
+    if sizes:
+        p, s, z = sizes
+    return struct.pack("<8sIiiiiiiIQQQ", magic, version, bits, E, K, N, group, asym, crc, p, s, z), p, s, z
+
+
+def test_packed_weights_file_header(ckl, tmp_path):
+    """The on-disk format of packed weights (ckl_moe_weights_file_info): the documented
+    64-byte header is read back field for field; wrong magic, version or section sizes
+    are refused; a payload that fails its checksum is refused before any device copy."""
+    hdr, p, s, z = _weights_header()
+    assert len(hdr) == 64
+    f = tmp_path / "w.bin"
+    f.write_bytes(hdr + bytes(p + 2 * s + 4 * z))
+    w = ckl.MoeWeights()
+    ckl.check(ckl.lib().ckl_moe_weights_file_info(str(f).encode(), C.byref(w)), "info")
+    assert (w.bits, w.E, w.K, w.N, w.group, w.asym) == (4, 2, 256, 128, 128, 1)
+    assert w.packed is None and w.scales is None
+    for bad in (_weights_header(magic=b"CKLMOEW0")[0], _weights_header(version=2)[0],
+                _weights_header(sizes=(p + 16, s, z))[0]):
+        g = tmp_path / "bad.bin"
+        g.write_bytes(bad + bytes(p + 2 * s + 4 * z))
+        assert ckl.lib().ckl_moe_weights_file_info(str(g).encode(), C.byref(w)) != 0
+    # checksum of an all-zero payload is not 0: the load stops at the check
+    w2 = ckl.MoeWeights(4, 2, 256, 128, 128, 1, 0x1000, 0x2000, 0x3000)
+    st = ckl.lib().ckl_moe_weights_load(str(f).encode(), C.byref(w2), None)
+    assert st == 1 and b"checksum" in ckl.lib().ckl_last_error_string()

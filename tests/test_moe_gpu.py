@@ -246,3 +246,29 @@ def test_config5_w8a16_moe_full_size(ckl, oracle, dev):
     assert rel_rms(out.float().cpu().numpy(), ref.cpu().numpy()) <= REL_RMS
     del gq, uq, dq
     torch.cuda.empty_cache()
+
+
+@pytest.mark.parametrize("mode", ["int4", "int8pc", "fp16", "int4sym"])
+def test_packed_weights_file_round_trip(ckl, oracle, dev, tmp_path, mode):
+    """ckl_moe_weights_save / _file_info / _load: the buffers come back bit for bit and the
+    layer computes the same output from the loaded weights."""
+    import torch
+    E, k, d, F, T = 8, 2, 256, 384, 5
+    gq, uq, dq = _layer_weights(ckl, oracle, dev, E, d, F, mode)
+    paths = [tmp_path / f"{n}.ckw" for n in ("gate", "up", "down")]
+    for q, pth in zip((gq, uq, dq), paths):
+        q.save(pth)
+    lq = [ckl.QuantWeights.load(pth, device=dev) for pth in paths]
+    for a, b in zip((gq, uq, dq), lq):
+        assert (a.bits, a.E, a.K, a.N, a.group, a.asym) == (b.bits, b.E, b.K, b.N, b.group, b.asym)
+        assert torch.equal(a.packed, b.packed)
+        if a.bits != 16:
+            assert torch.equal(a.scales, b.scales)
+        if a.asym:
+            assert torch.equal(a.zeros, b.zeros)
+    lg = T_(oracle.normal((T, E), seed=7, fp16=False), dev)
+    X = T_(oracle.normal((T, d), seed=8), dev)
+    ref = ckl.MoeLayer(gq, uq, dq).forward(lg, X, k)
+    got = ckl.MoeLayer(*lq).forward(lg, X, k)
+    torch.cuda.synchronize()
+    assert torch.equal(ref, got)
