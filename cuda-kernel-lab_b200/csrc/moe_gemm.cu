@@ -155,11 +155,14 @@ __device__ __forceinline__ bool consume_pass(const GemmArgs& a, const uint8_t* r
                     }
                 }
             }
+            // per-group parameters: accumulate the group apart and scale it; per-channel
+            // scales (applied in the epilogue) or none: accumulate into the pass directly
             float gacc0[NT][4], gacc1[NT][4];
 #pragma unroll
             for (int i = 0; i < NT; i++)
 #pragma unroll
-                for (int c = 0; c < 4; c++) gacc0[i][c] = gacc1[i][c] = 0.f;
+                for (int c = 0; c < 4; c++)
+                    if (C::EMBED) gacc0[i][c] = gacc1[i][c] = 0.f;
 #pragma unroll
             for (int kb = 0; kb < 4; kb++) {          // 32-wide k blocks of the group
                 uint4 xv[NT];
@@ -190,14 +193,16 @@ __device__ __forceinline__ bool consume_pass(const GemmArgs& a, const uint8_t* r
 #pragma unroll
                     for (int i = 0; i < NT; i++) {
                         const uint32_t b0 = hb ? xv[i].z : xv[i].x, b1 = hb ? xv[i].w : xv[i].y;
-                        mma_16816(gacc0[i], w0[0], w0[1], w0[2], w0[3], b0, b1);
-                        if (SWIGLU) mma_16816(gacc1[i], w1[0], w1[1], w1[2], w1[3], b0, b1);
+                        mma_16816(C::EMBED ? gacc0[i] : acc0[i], w0[0], w0[1], w0[2], w0[3], b0, b1);
+                        if (SWIGLU)
+                            mma_16816(C::EMBED ? gacc1[i] : acc1[i], w1[0], w1[1], w1[2], w1[3], b0, b1);
                     }
                 }
             }
             // group scale onto the fp32 accumulators (exact dequantisation up to fp32 rounding)
 #pragma unroll
             for (int i = 0; i < NT; i++) {
+                if (!C::EMBED) break;
                 acc0[i][0] += s_lo[0] * gacc0[i][0]; acc0[i][1] += s_lo[0] * gacc0[i][1];
                 acc0[i][2] += s_hi[0] * gacc0[i][2]; acc0[i][3] += s_hi[0] * gacc0[i][3];
                 if (SWIGLU) {
