@@ -57,7 +57,9 @@ def parse():
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="256x4096")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extras", action="store_true",
-                    help="skip the config-2 sweep and config-3 cascade rows")
+                    help="skip the extra rows (sweep, cascades, MoE, Mixtral, grouped GEMM)")
+    ap.add_argument("--extras", default="",
+                    help="comma-separated names of the extra rows to run (default: all)")
     return ap.parse_args()
 
 
@@ -419,6 +421,86 @@ def bench_cascade(ckl, dev, timer, peak):
                      "naive_equiv_GB/s": round(naive / (t_cas * 1e-3) / 1e9, 1),
                      "max_abs_diff_vs_plain": err, "prefix_chunks": cp.prefix_chunks,
                      "suffix_chunks": cp.suffix.num_chunks}
+        del d, ws, out, lse
+        torch.cuda.empty_cache()
+    return res
+
+
+def tree_batch(system, doc, n_groups, suffix, dev, seed):
+    """A shuffled paged batch shaped as a prefix tree: every sequence starts with the same
+    `system` tokens, the sequences of each of n_groups equal groups then share one `doc`-token
+    document, and each ends with its own suffix[b] tokens; filled U(-1,1) on the device."""
+    import numpy as np
+    import torch
+    suffix = np.asarray(suffix, np.int32)
+    B = len(suffix)
+    sp, dp = system // PAGE, doc // PAGE
+    spg = (suffix + PAGE - 1) // PAGE
+    total = sp + n_groups * dp + int(spg.sum())
+    perm = np.random.default_rng(seed).permutation(total).astype(np.int32)
+    lists, nxt = [], sp + n_groups * dp
+    for b in range(B):
+        g = b * n_groups // B
+        own = list(range(nxt, nxt + int(spg[b])))
+        nxt += int(spg[b])
+        lists.append(list(range(sp)) + list(range(sp + g * dp, sp + (g + 1) * dp)) + own)
+    indptr = np.zeros(B + 1, np.int32)
+    indptr[1:] = np.cumsum([len(x) for x in lists])
+    indices = perm[np.array([p for x in lists for p in x], np.int64)]
+    lens = (system + doc + suffix).astype(np.int32)
+    last = (suffix - (spg - 1) * PAGE).astype(np.int32)
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    k = torch.empty((total, PAGE, HKV, D), dtype=torch.float16, device=dev)
+    v = torch.empty_like(k)
+    _fill_uniform(k, g)
+    _fill_uniform(v, g)
+    q = (torch.rand((B, HQ, D), generator=g, device=dev) * 2 - 1).half()
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+    return (dict(q=q, k_cache=k, v_cache=v, kv_indptr=t(indptr), kv_indices=t(indices),
+                 kv_last_page_len=t(last)), (lens, indptr, indices), total)
+
+
+def bench_cascade_tree(ckl, dev, timer, peak):
+    """Prefix tree (the reference's cascade needs one prefix shared by the whole batch): 64
+    requests = a 1024-token system prompt shared by all, 4 groups of 16 sharing a
+    4096-token document each, private suffixes of 256 tokens (and U[1,1024]). The tree
+    cascade against the whole-batch cascade (which finds only the system prompt) and plain
+    split-KV on the same batch, cold L2."""
+    import numpy as np
+    import torch
+    res = {}
+    for name, suffix in (("64x(1024+4x4096+256)", np.full(64, 256)),
+                         ("64x(1024+4x4096+U[1,1024])",
+                          np.random.default_rng(78).integers(1, 1025, 64))):
+        d, (lens, indptr, indices), total = tree_batch(1024, 4096, 4, suffix, dev, seed=23)
+        base = ckl.make_params(**d, num_chunks=1, chunk_tokens=16)
+        tp = ckl.plan_cascade_tree(base, indptr, indices, lens, 256)
+        assert tp.use == 1 and tp.nodes == 5
+        cp = ckl.plan_cascade(base, indptr, indices, lens, 256)
+        nbytes = max(ckl.cascade_tree_workspace_size(tp), ckl.cascade_workspace_size(cp), 256)
+        ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+        out = torch.empty_like(d["q"])
+        lse = torch.empty((len(lens), HQ), dtype=torch.float32, device=dev)
+        t_tree = timer(lambda: ckl.cascade_tree_decode(tp, out=out, lse=lse, workspace=ws))
+        o_tree = out.clone()
+        t_cas = timer(lambda: ckl.cascade_decode(cp, out=out, lse=lse, workspace=ws))
+        t_plain = timer(lambda: ckl.decode_attention(**d, out=out, lse=lse))
+        err = float((o_tree.float() - out.float()).abs().max())
+        naive = algorithmic_bytes(lens)
+        unique = total * PAGE * HKV * D * 2 * 2 + len(lens) * HQ * (D * 4 + 4)
+        bound_ms = naive / (peak * 1e9) * 1e3
+        unique_ms = unique / (peak * 1e9) * 1e3
+        res[name] = {"ms_tree_cascade": round(t_tree, 4), "ms_whole_batch_cascade": round(t_cas, 4),
+                     "ms_plain_split_kv": round(t_plain, 4), "naive_bytes": naive,
+                     "unique_bytes": unique, "naive_bw_bound_ms": round(bound_ms, 4),
+                     "unique_bw_bound_ms": round(unique_ms, 4),
+                     "speedup_vs_bw_bound": round(bound_ms / t_tree, 2),
+                     "speedup_vs_plain": round(t_plain / t_tree, 2),
+                     "speedup_vs_whole_batch_cascade": round(t_cas / t_tree, 2),
+                     "unique_GB/s": round(unique / (t_tree * 1e-3) / 1e9, 1),
+                     "max_abs_diff_vs_plain": err, "tree_nodes": tp.nodes,
+                     "prefix_items_per_kv_head": tp.items, "suffix_chunks": tp.suffix.num_chunks}
         del d, ws, out, lse
         torch.cuda.empty_cache()
     return res
@@ -971,19 +1053,26 @@ def run_ours(args):
         del k, v
         torch.cuda.empty_cache()
         timer = ColdTimer(dev, world)
+        want = set(filter(None, args.extras.split(",")))
+        run = lambda name: not want or name in want
         if world == 1:
-            extras["config2_sweep"] = sweep_config2(ckl, dev, timer, peak)
-            extras["config3_cascade"] = bench_cascade(ckl, dev, timer, peak)
-            extras["config4_moe_w4a16_layer"] = bench_moe(ckl, dev, timer, peak)
-            extras["config5_mixtral_layer"] = bench_mixtral_layer(ckl, dev, timer, peak)
-            extras["grouped_gemm_tcgen05"] = bench_grouped_gemm(ckl, dev, timer, peak)
-            extras["decode_step_4_layers_config5"] = bench_decode_step(ckl, dev, timer, peak)
+            rows = (("config2_sweep", sweep_config2), ("config3_cascade", bench_cascade),
+                    ("prefix_tree_cascade", bench_cascade_tree),
+                    ("config4_moe_w4a16_layer", bench_moe),
+                    ("config5_mixtral_layer", bench_mixtral_layer),
+                    ("grouped_gemm_tcgen05", bench_grouped_gemm),
+                    ("decode_step_4_layers_config5", bench_decode_step))
+            for name, fn in rows:
+                if run(name):
+                    extras[name] = fn(ckl, dev, timer, peak)
         else:
             ex = ckl.torch_exchange()
-            extras["config4_moe_w4a16_layer_ep"] = bench_moe_ep(ckl, dev, timer, peak, rank,
-                                                                world, ex)
-            extras["config5_mixtral_layer_tp_ep"] = bench_mixtral_ep(ckl, dev, timer, peak,
-                                                                     rank, world, ex)
+            if run("config4_moe_w4a16_layer_ep"):
+                extras["config4_moe_w4a16_layer_ep"] = bench_moe_ep(ckl, dev, timer, peak, rank,
+                                                                    world, ex)
+            if run("config5_mixtral_layer_tp_ep"):
+                extras["config5_mixtral_layer_tp_ep"] = bench_mixtral_ep(ckl, dev, timer, peak,
+                                                                         rank, world, ex)
         extras["extras_timing"] = ("cold L2 (256 MB memset before each sample), median of 15"
                                    + ("; ranks start each sample together (barrier), max over "
                                       "ranks" if world > 1 else ""))

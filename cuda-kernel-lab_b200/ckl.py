@@ -20,6 +20,7 @@ HEAD_DIM = 128
 PAGE = 16
 
 CKL_OK = 0
+CKL_WORKSPACE_TOO_SMALL = 6
 STATUS = {0: "CKL_OK", 1: "CKL_INVALID_ARG", 2: "CKL_UNSUPPORTED_SHAPE", 3: "CKL_CUDA_ERROR",
           4: "CKL_NCCL_ERROR", 5: "CKL_TIMEOUT", 6: "CKL_WORKSPACE_TOO_SMALL"}
 
@@ -47,6 +48,13 @@ class CascadePlan(C.Structure):
                 ("prefix_chunks", C.c_int), ("prefix_chunk_tokens", C.c_int),
                 ("qtiles", C.c_int), ("prefix_page_ids", C.c_void_p),
                 ("suffix", DecodeParams)]
+
+
+class CascadeTreePlan(C.Structure):
+    """ckl_cascade_tree_plan_t (the prefix-tree cascade; no reference counterpart)."""
+    _fields_ = [("use", C.c_int), ("nodes", C.c_int), ("items", C.c_int),
+                ("chunk_pages", C.c_int), ("max_path_slots", C.c_int), ("reserved", C.c_int),
+                ("table_bytes", C.c_size_t), ("suffix", DecodeParams)]
 
 
 class MoeWeights(C.Structure):
@@ -104,6 +112,14 @@ _SIGS = {
     "ckl_cascade_workspace_size": (C.c_size_t, [C.POINTER(CascadePlan)]),
     "ckl_cascade_prefix": (C.c_int, [C.POINTER(CascadePlan), C.c_void_p, C.c_void_p,
                                      C.c_void_p]),
+    "ckl_prefix_tree": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p,
+                                  C.c_void_p, C.c_void_p]),
+    "ckl_cascade_tree_plan": (C.c_int, [C.POINTER(DecodeParams), C.c_void_p, C.c_void_p,
+                                        C.c_void_p, C.c_int, C.POINTER(CascadeTreePlan),
+                                        C.c_void_p, C.c_size_t]),
+    "ckl_cascade_tree_workspace_size": (C.c_size_t, [C.POINTER(CascadeTreePlan)]),
+    "ckl_cascade_tree_decode": (C.c_int, [C.POINTER(CascadeTreePlan), C.c_void_p, C.c_void_p,
+                                          C.c_void_p, C.c_void_p, C.c_size_t, C.c_void_p]),
     "ckl_cascade_decode": (C.c_int, [C.POINTER(CascadePlan), C.c_void_p, C.c_void_p,
                                      C.c_void_p, C.c_size_t, C.c_void_p]),
     "ckl_moe_packed_bytes": (C.c_size_t, [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int]),
@@ -408,6 +424,69 @@ def cascade_decode(cp: CascadePlan, out=None, lse=None, workspace=None, stream=N
     ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
     check(lib().ckl_cascade_decode(C.byref(cp), _ptr(out), _ptr(lse), _ptr(workspace), ws_bytes,
                                    _stream(stream)), "ckl_cascade_decode")
+    return out, lse
+
+
+def prefix_tree(indptr, indices, min_pages=1):
+    """ckl_prefix_tree on host int32 arrays -> (perm [B], nodes [n, 5] = {first page, end
+    page, m0, m1, parent}, start_pages [B])."""
+    import numpy as np
+    ip, ix = _np_i32(indptr), _np_i32(indices)
+    B = len(ip) - 1
+    perm = np.zeros(max(B, 1), np.int32)
+    start = np.zeros(max(B, 1), np.int32)
+    nodes = np.zeros((max(B - 1, 1), 5), np.int32)
+    vp = lambda a: a.ctypes.data_as(C.c_void_p)
+    n = lib().ckl_prefix_tree(vp(ip), vp(ix), B, min_pages, vp(perm), vp(nodes), vp(start))
+    if n < 0:
+        raise CklError(1, "ckl_prefix_tree", "bad page table")
+    return perm[:B], nodes[:n].copy(), start[:B]
+
+
+def plan_cascade_tree(base: DecodeParams, h_indptr, h_indices, h_lens, min_prefix=256):
+    """Plans the prefix-tree cascade from host copies of the page table and uploads its
+    tables (plan.tables, a device uint8 tensor)."""
+    import numpy as np
+    torch = _torch()
+    ip, ix, ln = _np_i32(h_indptr), _np_i32(h_indices), _np_i32(h_lens)
+    vp = lambda a: a.ctypes.data_as(C.c_void_p)
+    tp = CascadeTreePlan()
+    st = lib().ckl_cascade_tree_plan(C.byref(base), vp(ip), vp(ix), vp(ln), min_prefix,
+                                     C.byref(tp), None, 0)
+    tp.tables = None
+    if st == CKL_WORKSPACE_TOO_SMALL and tp.use:
+        host = np.zeros(tp.table_bytes, np.uint8)
+        check(lib().ckl_cascade_tree_plan(C.byref(base), vp(ip), vp(ix), vp(ln), min_prefix,
+                                          C.byref(tp), vp(host), host.nbytes),
+              "ckl_cascade_tree_plan")
+        dev = torch.device("cuda", torch.cuda.current_device())
+        tp.tables = torch.from_numpy(host).to(dev)
+    else:
+        check(st, "ckl_cascade_tree_plan")
+    tp._keep = (base,)
+    return tp
+
+
+def cascade_tree_workspace_size(tp: CascadeTreePlan):
+    return lib().ckl_cascade_tree_workspace_size(C.byref(tp))
+
+
+def cascade_tree_decode(tp: CascadeTreePlan, out=None, lse=None, workspace=None, stream=None):
+    """Prefix-tree cascade decode -> (out fp16 [B,Hq,128], lse fp32 [B,Hq])."""
+    torch = _torch()
+    sp = tp.suffix
+    dev = torch.device("cuda", torch.cuda.current_device())
+    if out is None:
+        out = torch.empty((sp.B, sp.Hq, HEAD_DIM), dtype=torch.float16, device=dev)
+    if lse is None:
+        lse = torch.empty((sp.B, sp.Hq), dtype=torch.float32, device=dev)
+    need = cascade_tree_workspace_size(tp)
+    if need and (workspace is None or workspace.numel() * workspace.element_size() < need):
+        workspace = torch.empty(need, dtype=torch.uint8, device=dev)
+    ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
+    check(lib().ckl_cascade_tree_decode(C.byref(tp), _ptr(tp.tables), _ptr(out), _ptr(lse),
+                                        _ptr(workspace), ws_bytes, _stream(stream)),
+          "ckl_cascade_tree_decode")
     return out, lse
 
 

@@ -16,7 +16,10 @@
 //   4. one LSE merge over prefix and suffix slots.
 
 #include <algorithm>
+#include <cstring>
 #include <mutex>
+#include <numeric>
+#include <vector>
 
 #include "attn_common.cuh"
 
@@ -35,6 +38,12 @@ constexpr int P_SMEM = 1024 + P_RING + 2 * PSTAGES * 8;
 struct PrefixArgs {
     const __half* q;
     const int* prefix_pages;
+    // prefix-tree mode (items != NULL): CTA x runs work item x, two int4 each:
+    //   {first page (index into kv_indices), pages, first member (position in perm), members},
+    //   {first stacked query row, partial slot, 0, 0}
+    const int4* items;
+    const int* indices;
+    const int* perm;
     float* part_o;
     float* part_lse;
     unsigned* err;
@@ -44,7 +53,9 @@ struct PrefixArgs {
 };
 
 // grid = (prefix chunks, ceil(B*G / 128), Hkv). Writes the normalised partial (o, lse) of
-// every stacked query row it covers into slot blockIdx.x.
+// every stacked query row it covers into slot blockIdx.x. Prefix-tree mode: grid = (work
+// items, 1, Hkv); item x covers a run of pages shared by the sequences perm[m0, m0 + members)
+// and its stacked rows [row0, row0 + 128) of members x G, written into the item's slot.
 __global__ void __launch_bounds__(PTHREADS, 1)
 cascade_prefix_kernel(const __grid_constant__ CUtensorMap tmK,
                       const __grid_constant__ CUtensorMap tmV, const PrefixArgs a) {
@@ -53,13 +64,31 @@ cascade_prefix_kernel(const __grid_constant__ CUtensorMap tmK,
     uint64_t* full = reinterpret_cast<uint64_t*>(ring + P_RING);
     uint64_t* empty = full + PSTAGES;
 
-    const int chunk = blockIdx.x, qtile = blockIdx.y, kvh = blockIdx.z;
+    const int kvh = blockIdx.z;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int kbeg = chunk * a.chunk_tokens;
-    const int kend = min(a.prefix_len, kbeg + a.chunk_tokens);
-    const int p0 = kbeg / PAGE;
-    const int npg = kend > kbeg ? (kend - kbeg + PAGE - 1) / PAGE : 0;
-    const int nq = a.B * a.G;
+    const int* pages;          // this CTA's run of physical page ids
+    int npg, kend;             // pages, and keys of the run (tokens from its first page)
+    int nq, row0, m0, slot;    // stacked rows, first row of this tile, first member, slot
+    if (a.items) {
+        const int4 w0 = __ldg(a.items + 2 * blockIdx.x), w1 = __ldg(a.items + 2 * blockIdx.x + 1);
+        pages = a.indices + w0.x;
+        npg = w0.y;
+        kend = npg * PAGE;     // shared runs never hold a sequence's last page: all full
+        m0 = w0.z;
+        nq = w0.w * a.G;
+        row0 = w1.x;
+        slot = w1.y;
+    } else {
+        const int kbeg = blockIdx.x * a.chunk_tokens;
+        const int kstop = min(a.prefix_len, kbeg + a.chunk_tokens);
+        pages = a.prefix_pages + kbeg / PAGE;
+        npg = kstop > kbeg ? (kstop - kbeg + PAGE - 1) / PAGE : 0;
+        kend = kstop - kbeg;
+        m0 = 0;
+        nq = a.B * a.G;
+        row0 = blockIdx.y * PROWS;
+        slot = blockIdx.x;
+    }
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < PSTAGES; s++) {
@@ -83,7 +112,7 @@ cascade_prefix_kernel(const __grid_constant__ CUtensorMap tmK,
         int ok = 1, issued = 0;
         for (int base = 0; base < npg && ok; base += 32) {
             const int cnt = min(32, npg - base);
-            const int my_page = lane < cnt ? __ldg(a.prefix_pages + p0 + base + lane) : 0;
+            const int my_page = lane < cnt ? __ldg(pages + base + lane) : 0;
             for (int j = 0; j < cnt; j++) {
                 const int page = __shfl_sync(0xffffffffu, my_page, j);
                 if (lane == 0) {
@@ -110,12 +139,18 @@ cascade_prefix_kernel(const __grid_constant__ CUtensorMap tmK,
 
     // -------------------------------------------------------------------- consumer warps
     const int g = lane >> 2, t = lane & 3;
-    const int r_lo = qtile * PROWS + warp * 16 + g, r_hi = r_lo + 8;
+    const int r_lo = row0 + warp * 16 + g, r_hi = r_lo + 8;
     const bool ok_lo = r_lo < nq, ok_hi = r_hi < nq;
-    const bool active = qtile * PROWS + warp * 16 < nq;   // warp-uniform
+    const bool active = row0 + warp * 16 < nq;   // warp-uniform
     size_t qrow_lo = 0, qrow_hi = 0;
-    if (ok_lo) qrow_lo = (size_t)(r_lo / a.G) * a.Hq + (size_t)kvh * a.G + r_lo % a.G;
-    if (ok_hi) qrow_hi = (size_t)(r_hi / a.G) * a.Hq + (size_t)kvh * a.G + r_hi % a.G;
+    if (ok_lo) {
+        const int seq = a.perm ? __ldg(a.perm + m0 + r_lo / a.G) : r_lo / a.G;
+        qrow_lo = (size_t)seq * a.Hq + (size_t)kvh * a.G + r_lo % a.G;
+    }
+    if (ok_hi) {
+        const int seq = a.perm ? __ldg(a.perm + m0 + r_hi / a.G) : r_hi / a.G;
+        qrow_hi = (size_t)seq * a.Hq + (size_t)kvh * a.G + r_hi % a.G;
+    }
 
     uint32_t qa0[8], qa1[8], qa2[8], qa3[8];
 #pragma unroll
@@ -161,7 +196,7 @@ cascade_prefix_kernel(const __grid_constant__ CUtensorMap tmK,
                 mma_16816(sc[0], qa0[kk], qa1[kk], qa2[kk], qa3[kk], b00, b01);
                 mma_16816(sc[1], qa0[kk], qa1[kk], qa2[kk], qa3[kk], b10, b11);
             }
-            const int kbase = (p0 + i) * PAGE;
+            const int kbase = i * PAGE;
             if (kbase + PAGE > kend) {
 #pragma unroll
                 for (int n = 0; n < 2; n++)
@@ -223,20 +258,20 @@ cascade_prefix_kernel(const __grid_constant__ CUtensorMap tmK,
     if (!ok) { l_lo = l_hi = 0.f; }
     const float inv_lo = l_lo > 0.f ? 1.f / l_lo : 0.f, inv_hi = l_hi > 0.f ? 1.f / l_hi : 0.f;
     if (ok_lo) {
-        const size_t slot = qrow_lo * a.part_stride + chunk;
-        float* dst = a.part_o + slot * D + 2 * t;
+        const size_t pslot = qrow_lo * a.part_stride + slot;
+        float* dst = a.part_o + pslot * D + 2 * t;
 #pragma unroll
         for (int j = 0; j < 16; j++)
             *reinterpret_cast<float2*>(dst + 8 * j) = make_float2(o[j][0] * inv_lo, o[j][1] * inv_lo);
-        if (t == 0) a.part_lse[slot] = l_lo > 0.f ? (m_lo + lg2(l_lo)) * LN2 : -INFINITY;
+        if (t == 0) a.part_lse[pslot] = l_lo > 0.f ? (m_lo + lg2(l_lo)) * LN2 : -INFINITY;
     }
     if (ok_hi) {
-        const size_t slot = qrow_hi * a.part_stride + chunk;
-        float* dst = a.part_o + slot * D + 2 * t;
+        const size_t pslot = qrow_hi * a.part_stride + slot;
+        float* dst = a.part_o + pslot * D + 2 * t;
 #pragma unroll
         for (int j = 0; j < 16; j++)
             *reinterpret_cast<float2*>(dst + 8 * j) = make_float2(o[j][2] * inv_hi, o[j][3] * inv_hi);
-        if (t == 0) a.part_lse[slot] = l_hi > 0.f ? (m_hi + lg2(l_hi)) * LN2 : -INFINITY;
+        if (t == 0) a.part_lse[pslot] = l_hi > 0.f ? (m_hi + lg2(l_hi)) * LN2 : -INFINITY;
     }
 }
 
@@ -268,7 +303,7 @@ ckl_status launch_prefix(const ckl_cascade_plan_t* cp, float* part_o, float* par
     CUtensorMap tmK, tmV;
     ckl_status st = encode_kv_maps(b.k_cache, b.v_cache, b.Hkv, b.num_pages, &tmK, &tmV);
     if (st != CKL_OK) return st;
-    PrefixArgs a;
+    PrefixArgs a{};
     a.q = static_cast<const __half*>(b.q);
     a.prefix_pages = cp->prefix_page_ids;
     a.part_o = part_o;
@@ -302,6 +337,53 @@ ckl_status check_plan(const ckl_cascade_plan_t* cp) {
         return fail(CKL_INVALID_ARG, "cascade plan: qtiles do not cover B*G query rows");
     if (cp->prefix_chunks > 0x7fffffff / 1 || cp->qtiles > 65535 || cp->suffix.Hkv > 65535)
         return fail(CKL_UNSUPPORTED_SHAPE, "cascade grid too large");
+    return CKL_OK;
+}
+
+// ------------------------------------------------------------------ prefix tree
+// Device tables of the tree cascade, one buffer: seq_tab int2[B] {private suffix start in
+// tokens, first suffix slot}, perm int[B], then the prefix work items, 2 x int4 each.
+struct TreeTables {
+    size_t perm, items, bytes;
+};
+TreeTables tree_tables(int B, int items) {
+    TreeTables t;
+    t.perm = align_up((size_t)B * 8, 16);
+    t.items = t.perm + align_up((size_t)B * 4, 16);
+    t.bytes = t.items + (size_t)items * 32;
+    return t;
+}
+
+ckl_status launch_tree_prefix(const ckl_cascade_tree_plan_t* tp, const uint8_t* tables,
+                              float* part_o, float* part_lse, cudaStream_t stream) {
+    const ckl_decode_params& b = tp->suffix;
+    const DeviceInfo* di = device_info();
+    if (!di) return CKL_CUDA_ERROR;
+    const PrefixSetup* ps = setup(di);
+    if (ps->st != CKL_OK) return ps->st;
+    CUtensorMap tmK, tmV;
+    ckl_status st = encode_kv_maps(b.k_cache, b.v_cache, b.Hkv, b.num_pages, &tmK, &tmV);
+    if (st != CKL_OK) return st;
+    const TreeTables tt = tree_tables(b.B, tp->items);
+    PrefixArgs a{};
+    a.q = static_cast<const __half*>(b.q);
+    a.items = reinterpret_cast<const int4*>(tables + tt.items);
+    a.indices = b.kv_indices;
+    a.perm = reinterpret_cast<const int*>(tables + tt.perm);
+    a.part_o = part_o;
+    a.part_lse = part_lse;
+    a.err = di->err_word;
+    a.timeout_ns = spin_timeout_ns();
+    a.B = b.B;
+    a.Hq = b.Hq;
+    a.Hkv = b.Hkv;
+    a.G = b.Hq / b.Hkv;
+    a.part_stride = b.part_stride;
+    a.scale_log2 = b.sm_scale * LOG2E;
+    void* args[] = {&tmK, &tmV, &a};
+    dim3 grid((unsigned)tp->items, 1, (unsigned)b.Hkv);
+    CKL_CUDA_TRY(cudaLaunchKernel(reinterpret_cast<const void*>(cascade_prefix_kernel), grid,
+                                  dim3(PTHREADS), args, P_SMEM, stream));
     return CKL_OK;
 }
 
@@ -390,6 +472,235 @@ ckl_status ckl_cascade_prefix(const ckl_cascade_plan_t* plan, float* part_o, flo
     if (st != CKL_OK || plan->suffix.B == 0) return st;
     if (!part_o || !part_lse) return fail(CKL_INVALID_ARG, "cascade_prefix: NULL partials");
     return launch_prefix(plan, part_o, part_lse, (cudaStream_t)stream);
+}
+
+int ckl_prefix_tree(const int* ip, const int* ix, int B, int min_pages, int* perm, int* nodes,
+                    int* start_pages) {
+    if (!ip || B < 0 || (B > 0 && (!ix || !perm || !start_pages)) || (B > 1 && !nodes)) return -1;
+    for (int b = 0; b < B; b++)
+        if (ip[b + 1] < ip[b]) return -1;
+    min_pages = std::max(1, min_pages);
+    // key of b: its page ids but the last (which stays private)
+    auto klen = [&](int b) { return std::max(0, ip[b + 1] - ip[b] - 1); };
+    std::vector<int> order(B);
+    std::iota(order.begin(), order.end(), 0);
+    std::stable_sort(order.begin(), order.end(), [&](int x, int y) {
+        const int lx = klen(x), ly = klen(y), n = std::min(lx, ly);
+        for (int i = 0; i < n; i++) {
+            const int px = ix[ip[x] + i], py = ix[ip[y] + i];
+            if (px != py) return px < py;
+        }
+        return lx < ly;
+    });
+    for (int i = 0; i < B; i++) {
+        perm[i] = order[i];
+        start_pages[i] = 0;
+    }
+    if (B < 2) return 0;
+    auto lcp = [&](int x, int y) {
+        const int n = std::min(klen(x), klen(y));
+        int i = 0;
+        while (i < n && ix[ip[x] + i] == ix[ip[y] + i]) i++;
+        return i;
+    };
+    // Every interval [lb, rb] of sorted positions whose keys share their first l > 0 pages
+    // (and that no longer run extends) is a trie node; one stack pass over the adjacent
+    // common-prefix lengths finds them all with their parents.
+    struct Iv { int l, lb, rb, parent; };
+    struct Open { int l, lb, id; };
+    std::vector<Iv> iv;
+    std::vector<Open> stk{{0, 0, -1}};
+    for (int i = 1; i <= B; i++) {
+        const int cur = i < B ? lcp(order[i - 1], order[i]) : 0;
+        int lb = i - 1, last = -1;
+        while (cur < stk.back().l) {
+            const Open top = stk.back();
+            stk.pop_back();
+            iv[top.id].rb = i - 1;
+            lb = top.lb;
+            last = top.id;
+            if (cur <= stk.back().l) {
+                iv[last].parent = stk.back().id;
+                last = -1;
+            }
+        }
+        if (cur > stk.back().l) {
+            const int id = (int)iv.size();
+            iv.push_back({cur, lb, -1, -1});
+            if (last >= 0) iv[last].parent = id;
+            stk.push_back({cur, lb, id});
+        }
+    }
+    // parents before children; keep nodes whose own run (from the nearest kept ancestor) is
+    // long enough
+    std::vector<int> pre((size_t)iv.size());
+    std::iota(pre.begin(), pre.end(), 0);
+    std::sort(pre.begin(), pre.end(), [&](int x, int y) {
+        return iv[x].lb != iv[y].lb ? iv[x].lb < iv[y].lb : iv[x].rb > iv[y].rb;
+    });
+    std::vector<int> out_id(iv.size(), -1), kept_anc(iv.size(), -1);
+    int n = 0;
+    for (int id : pre) {
+        const int par = iv[id].parent;
+        kept_anc[id] = par < 0 ? -1 : (out_id[par] >= 0 ? par : kept_anc[par]);
+        const int first = kept_anc[id] < 0 ? 0 : iv[kept_anc[id]].l;
+        if (iv[id].l - first < min_pages) continue;
+        out_id[id] = n;
+        int* nd = nodes + 5 * n;
+        nd[0] = first;
+        nd[1] = iv[id].l;
+        nd[2] = iv[id].lb;
+        nd[3] = iv[id].rb + 1;
+        nd[4] = kept_anc[id] < 0 ? -1 : out_id[kept_anc[id]];
+        for (int i = iv[id].lb; i <= iv[id].rb; i++) start_pages[order[i]] = iv[id].l;
+        n++;
+    }
+    return n;
+}
+
+ckl_status ckl_cascade_tree_plan(const ckl_decode_params* base, const int* h_indptr,
+                                 const int* h_indices, const int* h_lens, int min_prefix,
+                                 ckl_cascade_tree_plan_t* plan, void* tables, size_t table_bytes) {
+    if (!plan || !base || !h_indptr || !h_indices || !h_lens)
+        return fail(CKL_INVALID_ARG, "cascade_tree_plan: NULL");
+    int G = 0;
+    ckl_status st = attn::validate(base, &G);
+    if (st != CKL_OK) return st;
+    *plan = ckl_cascade_tree_plan_t{};
+    plan->suffix = *base;
+    const int B = base->B;
+    std::vector<int> perm(std::max(B, 1)), nodes(5 * (size_t)std::max(B - 1, 1)), start(std::max(B, 1));
+    const int n = ckl_prefix_tree(h_indptr, h_indices, B, ceil_div(std::max(min_prefix, 1), PAGE),
+                                  perm.data(), nodes.data(), start.data());
+    if (n < 0) return fail(CKL_INVALID_ARG, "cascade_tree_plan: bad page table");
+    int max_len = 0;
+    for (int b = 0; b < B; b++) max_len = std::max(max_len, h_lens[b]);
+    if (n == 0) {
+        plan->use = 0;
+        st = ckl_decode_plan(G, B, base->Hkv, max_len, 0, &plan->suffix.num_chunks,
+                             &plan->suffix.chunk_tokens);
+        plan->suffix.kv_start = 0;
+        plan->suffix.chunk_base = 0;
+        plan->suffix.part_stride = plan->suffix.num_chunks;
+        return st;
+    }
+    const DeviceInfo* di = device_info();
+    if (!di) return CKL_CUDA_ERROR;
+    const PrefixSetup* ps = setup(di);
+    if (ps->st != CKL_OK) return ps->st;
+    // about one wave of prefix CTAs over all nodes, >= 16 pages (256 tokens) per work item
+    long long work = 0;
+    for (int i = 0; i < n; i++) {
+        const int* nd = &nodes[5 * i];
+        work += (long long)(nd[1] - nd[0]) * ceil_div((nd[3] - nd[2]) * G, PROWS);
+    }
+    const long long target = std::max(1LL, (long long)di->sms * std::max(1, ps->per_sm) / base->Hkv);
+    const int cp = (int)std::max(16LL, (work + target - 1) / target);
+    // slots: a node's chunks follow its kept ancestors' chunks
+    std::vector<int> nchunks(n), slot0(n);
+    int items = 0;
+    for (int i = 0; i < n; i++) {
+        const int* nd = &nodes[5 * i];
+        nchunks[i] = ceil_div(nd[1] - nd[0], cp);
+        slot0[i] = nd[4] < 0 ? 0 : slot0[nd[4]] + nchunks[nd[4]];
+        items += nchunks[i] * ceil_div((nd[3] - nd[2]) * G, PROWS);
+    }
+    // per sequence: first suffix slot = end of its deepest node's slots
+    std::vector<int> suffix_slot(B, 0);
+    for (int i = 0; i < n; i++) {
+        const int* nd = &nodes[5 * i];
+        for (int m = nd[2]; m < nd[3]; m++) suffix_slot[perm[m]] = slot0[i] + nchunks[i];
+    }
+    int max_path = 0, max_suffix = 1;
+    for (int b = 0; b < B; b++) {
+        max_path = std::max(max_path, suffix_slot[b]);
+        max_suffix = std::max(max_suffix, h_lens[b] - start[b] * PAGE);
+    }
+    plan->use = 1;
+    plan->nodes = n;
+    plan->items = items;
+    plan->chunk_pages = cp;
+    plan->max_path_slots = max_path;
+    st = ckl_decode_plan(G, B, base->Hkv, max_suffix, 0, &plan->suffix.num_chunks,
+                         &plan->suffix.chunk_tokens);
+    if (st != CKL_OK) return st;
+    plan->suffix.kv_start = 0;
+    plan->suffix.chunk_base = 0;
+    plan->suffix.part_stride = max_path + plan->suffix.num_chunks;
+    const TreeTables tt = tree_tables(B, items);
+    plan->table_bytes = tt.bytes;
+    if (!tables || table_bytes < tt.bytes)
+        return fail(CKL_WORKSPACE_TOO_SMALL, "cascade_tree_plan: tables need %zu bytes, got %zu",
+                    tt.bytes, tables ? table_bytes : (size_t)0);
+    uint8_t* tb = static_cast<uint8_t*>(tables);
+    memset(tb, 0, tt.bytes);
+    int* seq_tab = reinterpret_cast<int*>(tb);
+    for (int b = 0; b < B; b++) {
+        seq_tab[2 * b] = start[b] * PAGE;
+        seq_tab[2 * b + 1] = suffix_slot[b];
+    }
+    memcpy(tb + tt.perm, perm.data(), (size_t)B * 4);
+    int* it = reinterpret_cast<int*>(tb + tt.items);
+    for (int i = 0; i < n; i++) {
+        const int* nd = &nodes[5 * i];
+        const int members = nd[3] - nd[2], run = nd[1] - nd[0];
+        const int page0 = h_indptr[perm[nd[2]]] + nd[0];
+        for (int c = 0; c < nchunks[i]; c++)
+            for (int row0 = 0; row0 < members * G; row0 += PROWS) {
+                it[0] = page0 + c * cp;
+                it[1] = std::min(cp, run - c * cp);
+                it[2] = nd[2];
+                it[3] = members;
+                it[4] = row0;
+                it[5] = slot0[i] + c;
+                it += 8;
+            }
+    }
+    return CKL_OK;
+}
+
+size_t ckl_cascade_tree_workspace_size(const ckl_cascade_tree_plan_t* plan) {
+    if (!plan) return 0;
+    if (!plan->use) return ckl_decode_workspace_size(&plan->suffix);
+    const ckl_decode_params& s = plan->suffix;
+    return attn::part_o_bytes(&s) + align_up((size_t)s.B * s.Hq * s.part_stride * sizeof(float), 256);
+}
+
+ckl_status ckl_cascade_tree_decode(const ckl_cascade_tree_plan_t* plan, const void* d_tables,
+                                   void* out, float* lse, void* workspace, size_t workspace_bytes,
+                                   void* stream) {
+    if (!plan) return fail(CKL_INVALID_ARG, "cascade tree plan is NULL");
+    if (!plan->use)
+        return ckl_decode_attention(&plan->suffix, out, lse, workspace, workspace_bytes, stream);
+    const ckl_decode_params& sp = plan->suffix;
+    int G = 0;
+    ckl_status st = attn::validate(&sp, &G);
+    if (st != CKL_OK || sp.B == 0) return st;
+    if (plan->nodes <= 0 || plan->items <= 0 || plan->chunk_pages <= 0 || plan->max_path_slots <= 0 ||
+        sp.kv_start != 0 || sp.chunk_base != 0 ||
+        sp.part_stride != plan->max_path_slots + sp.num_chunks ||
+        plan->table_bytes != tree_tables(sp.B, plan->items).bytes)
+        return fail(CKL_INVALID_ARG, "inconsistent cascade tree plan");
+    if (!d_tables || ((uintptr_t)d_tables & 15))
+        return fail(CKL_INVALID_ARG, "cascade_tree_decode: tables must be 16-byte aligned device memory");
+    if (!out || !lse) return fail(CKL_INVALID_ARG, "cascade_tree_decode: out/lse are NULL");
+    if ((uintptr_t)out & 7) return fail(CKL_INVALID_ARG, "out needs 8-byte alignment");
+    const size_t need = ckl_cascade_tree_workspace_size(plan);
+    if (!workspace || workspace_bytes < need)
+        return fail(CKL_WORKSPACE_TOO_SMALL, "cascade_tree_decode needs %zu workspace bytes, got %zu",
+                    need, workspace_bytes);
+    if ((uintptr_t)workspace & 255) return fail(CKL_INVALID_ARG, "workspace must be 256-byte aligned");
+    const cudaStream_t s = (cudaStream_t)stream;
+    const uint8_t* tables = static_cast<const uint8_t*>(d_tables);
+    const int2* seq_tab = reinterpret_cast<const int2*>(tables);
+    float* part_o = static_cast<float*>(workspace);
+    float* part_lse = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + attn::part_o_bytes(&sp));
+    st = launch_tree_prefix(plan, tables, part_o, part_lse, s);
+    if (st != CKL_OK) return st;
+    st = attn::launch_partial(&sp, G, false, nullptr, nullptr, part_o, part_lse, s, 0, 0, true, seq_tab);
+    if (st != CKL_OK) return st;
+    return attn::launch_merge(part_o, part_lse, static_cast<__half*>(out), lse, sp.B * sp.Hq,
+                              sp.part_stride, sp.Hq, sp.Hq, 0, seq_tab, sp.num_chunks, s);
 }
 
 ckl_status ckl_cascade_decode(const ckl_cascade_plan_t* plan, void* out, float* lse,

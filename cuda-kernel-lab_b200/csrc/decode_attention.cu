@@ -53,6 +53,7 @@ struct Args {
     unsigned long long timeout_ns;
     int B, Hq, Hkv, chunk_tokens, kv_start, chunk_base, part_stride, direct;
     int out_heads, head_offset;   // direct mode: row (b, h) goes to out row b*out_heads + head_offset + h
+    const int2* seq_tab;          // per sequence {kv_start, chunk_base}; NULL: the uniform fields
     float scale_log2;
 };
 
@@ -77,7 +78,8 @@ decode_partial_kernel(const __grid_constant__ CUtensorMap tmK,
     const int page_beg = __ldg(a.indptr + b);
     const int npages = __ldg(a.indptr + b + 1) - page_beg;
     const int seq_len = npages > 0 ? (npages - 1) * PAGE + __ldg(a.last + b) : 0;
-    const int kbeg = a.kv_start + chunk * a.chunk_tokens;       // multiple of 16
+    const int kv_start = a.seq_tab ? __ldg(&a.seq_tab[b].x) : a.kv_start;
+    const int kbeg = kv_start + chunk * a.chunk_tokens;         // multiple of 16
     const int kend = min(seq_len, kbeg + a.chunk_tokens);
     const int p0 = kbeg / PAGE;
     const int npg = kend > kbeg ? (kend - kbeg + PAGE - 1) / PAGE : 0;
@@ -203,7 +205,8 @@ decode_partial_kernel(const __grid_constant__ CUtensorMap tmK,
             a.out[orow * D + d] = __float2half_rn(val);
             if (d == 0) a.lse[orow] = lse_v;
         } else {
-            const size_t slot = row * a.part_stride + a.chunk_base + chunk;
+            const int cbase = a.seq_tab ? __ldg(&a.seq_tab[b].y) : a.chunk_base;
+            const size_t slot = row * a.part_stride + cbase + chunk;
             a.part_o[slot * D + d] = val;
             if (d == 0) a.part_lse[slot] = lse_v;
         }
@@ -216,23 +219,28 @@ decode_partial_kernel(const __grid_constant__ CUtensorMap tmK,
 // LSE merge: one warp per (sequence, q head) row, 4 dims per lane (16-byte loads). Row
 // r = b*Hq + h is written to out row b*out_heads + head_offset + h (identity when
 // out_heads = Hq and head_offset = 0; a head shard of a wider, possibly peer-mapped, output
-// otherwise).
+// otherwise). Rows are `stride` slots apart; a row of sequence b merges its first
+// seq_tab[b].y + tail slots (the prefix-tree cascade, whose sequences own different numbers
+// of slots), or all `stride` when seq_tab is NULL.
 __global__ void __launch_bounds__(256)
 merge_states_kernel(const float* __restrict__ part_o, const float* __restrict__ part_lse,
-                    __half* __restrict__ out, float* __restrict__ lse_out, int rows, int slots,
-                    int Hq, int out_heads, int head_offset) {
+                    __half* __restrict__ out, float* __restrict__ lse_out, int rows, int stride,
+                    int Hq, int out_heads, int head_offset, const int2* __restrict__ seq_tab,
+                    int tail) {
     pdl_wait();                      // partials of the kernel(s) before us
     const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (row >= rows) return;
-    const size_t orow = (size_t)(row / Hq) * out_heads + head_offset + row % Hq;
-    const float* L = part_lse + (size_t)row * slots;
+    const int b = row / Hq;
+    const size_t orow = (size_t)b * out_heads + head_offset + row % Hq;
+    const int slots = seq_tab ? min(stride, seq_tab[b].y + tail) : stride;
+    const float* L = part_lse + (size_t)row * stride;
     float m = -INFINITY;
     for (int c = lane; c < slots; c += 32) m = fmaxf(m, L[c]);
     m = warp_max(m);
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
     float wsum = 0.f;
     if (m != -INFINITY) {
-        const float4* po = reinterpret_cast<const float4*>(part_o + (size_t)row * slots * D) + lane;
+        const float4* po = reinterpret_cast<const float4*>(part_o + (size_t)row * stride * D) + lane;
 #pragma unroll 4
         for (int c = 0; c < slots; c++) {
             const float w = ex2((L[c] - m) * LOG2E);
@@ -321,7 +329,7 @@ ckl_status validate(const ckl_decode_params* p, int* G) {
 
 ckl_status launch_partial(const ckl_decode_params* p, int G, bool direct, __half* out,
                           float* lse, float* part_o, float* part_lse, cudaStream_t stream,
-                          int out_heads, int head_offset, bool pdl) {
+                          int out_heads, int head_offset, bool pdl, const int2* seq_tab) {
     const DeviceInfo* di = device_info();
     if (!di) return CKL_CUDA_ERROR;
     const KernelSetup* ks = setup(di);
@@ -352,11 +360,22 @@ ckl_status launch_partial(const ckl_decode_params* p, int G, bool direct, __half
     a.direct = direct ? 1 : 0;
     a.out_heads = out_heads > 0 ? out_heads : p->Hq;
     a.head_offset = head_offset;
+    a.seq_tab = seq_tab;
     a.scale_log2 = p->sm_scale * LOG2E;
 
     void* args[] = {&tmK, &tmV, &a};
     dim3 grid((unsigned)(p->B * p->Hkv), (unsigned)p->num_chunks);
     CKL_CUDA_TRY(launch(pick(G), grid, dim3(THREADS), SMEM_BYTES, stream, args, pdl));
+    return CKL_OK;
+}
+
+ckl_status launch_merge(const float* part_o, const float* part_lse, __half* out, float* lse,
+                        int rows, int stride, int Hq, int out_heads, int head_offset,
+                        const int2* seq_tab, int tail, cudaStream_t stream) {
+    void* args[] = {&part_o, &part_lse, &out, &lse, &rows, &stride, &Hq, &out_heads, &head_offset,
+                    &seq_tab, &tail};
+    CKL_CUDA_TRY(launch(reinterpret_cast<const void*>(merge_states_kernel), dim3(ceil_div(rows, 8)),
+                        dim3(256), 0, stream, args, true));
     return CKL_OK;
 }
 
@@ -424,12 +443,8 @@ ckl_status ckl_merge_states(const float* part_o, const float* part_lse, void* ou
     if (!part_o || !part_lse || !out || !lse) return fail(CKL_INVALID_ARG, "merge_states: NULL");
     if (((uintptr_t)part_o & 15) || ((uintptr_t)out & 7))
         return fail(CKL_INVALID_ARG, "merge_states: part_o 16-byte / out 8-byte alignment");
-    int rows_v = rows, slots_v = num_slots, one = 1, zero = 0;
-    __half* out_h = static_cast<__half*>(out);
-    void* args[] = {&part_o, &part_lse, &out_h, &lse, &rows_v, &slots_v, &one, &one, &zero};
-    CKL_CUDA_TRY(launch(reinterpret_cast<const void*>(merge_states_kernel), dim3(ceil_div(rows, 8)),
-                        dim3(256), 0, (cudaStream_t)stream, args, true));
-    return CKL_OK;
+    return launch_merge(part_o, part_lse, static_cast<__half*>(out), lse, rows, num_slots, 1, 1, 0,
+                        nullptr, 0, (cudaStream_t)stream);
 }
 
 }  // extern "C"
@@ -458,12 +473,8 @@ ckl_status decode_attention_rows(const ckl_decode_params* p, void* out, float* l
     float* part_lse = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + part_o_bytes(p));
     st = launch_partial(p, G, false, nullptr, nullptr, part_o, part_lse, s, 0, 0);
     if (st != CKL_OK) return st;
-    int rows = p->B * p->Hq, slots = p->part_stride, Hq = p->Hq;
-    __half* out_h = static_cast<__half*>(out);
-    void* args[] = {&part_o, &part_lse, &out_h, &lse, &rows, &slots, &Hq, &out_heads, &head_offset};
-    CKL_CUDA_TRY(launch(reinterpret_cast<const void*>(merge_states_kernel), dim3(ceil_div(rows, 8)),
-                        dim3(256), 0, s, args, true));
-    return CKL_OK;
+    return launch_merge(part_o, part_lse, static_cast<__half*>(out), lse, p->B * p->Hq, p->part_stride,
+                        p->Hq, out_heads > 0 ? out_heads : p->Hq, head_offset, nullptr, 0, s);
 }
 
 }  // namespace attn

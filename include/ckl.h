@@ -205,6 +205,64 @@ CKL_API ckl_status ckl_cascade_prefix(const ckl_cascade_plan_t* plan, float* par
 CKL_API ckl_status ckl_cascade_decode(const ckl_cascade_plan_t* plan, void* out, float* lse,
                                       void* workspace, size_t workspace_bytes, void* stream);
 
+/* --------------------------------------------------------------------------------------
+ * Prefix-tree cascade. No reference counterpart: the reference lists "a prefix tree where
+ * only a subset shares the prefix" as not done (README.md:73) and its cascade needs every
+ * sequence of the batch to share one prefix (shared_prefix_pages, 01:636-646). Here any
+ * group of >= 2 sequences whose page lists start with the same physical pages shares a tree
+ * node, nodes nest (a system prompt shared by all, a document shared by some), and each node
+ * is read once per kv head for all of its members' query heads.
+ * ------------------------------------------------------------------------------------ */
+
+/* Host only. The compressed trie of the batch's page lists, each sequence keeping its last
+ * page private. A node is a run of pages [first, end) that the sequences at positions
+ * [m0, m1) of perm share (>= 2 of them), begins where its nearest kept ancestor ends, and is
+ * kept when it holds >= min_pages pages (runs that are shorter fall to the node's children
+ * or its members' private suffixes). Writes:
+ *   perm[B]            sequences in trie order (every node's members are contiguous),
+ *   nodes[5 * n]       {first page, end page, m0, m1, parent node or -1}, parents first;
+ *                      room for max(B - 1, 1) nodes,
+ *   start_pages[B]     pages of sequence b covered by its nodes (its private suffix begins
+ *                      there; 0 when it is in no node).
+ * Returns n, or -1 for bad arguments. */
+CKL_API int ckl_prefix_tree(const int* h_indptr, const int* h_indices, int B, int min_pages,
+                            int* perm, int* nodes, int* start_pages);
+
+typedef struct ckl_cascade_tree_plan_t {
+    int use;              /* 0: no node kept; `suffix` is then the plain split-KV plan */
+    int nodes;            /* tree nodes kept */
+    int items;            /* prefix work items per kv head (node, page chunk, query tile) */
+    int chunk_pages;      /* pages per prefix work item, at most */
+    int max_path_slots;   /* prefix partial slots of the sequence with the most */
+    int reserved;
+    size_t table_bytes;   /* bytes of the device tables ckl_cascade_tree_decode reads */
+    ckl_decode_params suffix;   /* the private suffixes: per-sequence start and first slot
+                                   come from the tables (kv_start = chunk_base = 0 here);
+                                   part_stride = max_path_slots + num_chunks */
+} ckl_cascade_tree_plan_t;
+
+/* Host only. Plans the tree cascade from host copies of the page table (h_lens = sequence
+ * lengths in tokens) and writes its device tables into the HOST buffer `tables`
+ * (table_bytes bytes), which the caller copies to device memory (16-byte aligned) before
+ * ckl_cascade_tree_decode. Nodes are kept from min_prefix tokens. When `tables` is NULL or
+ * smaller than plan->table_bytes the plan is filled and CKL_WORKSPACE_TOO_SMALL returned.
+ * Prefix work items fill about one wave, >= 16 pages each. */
+CKL_API ckl_status ckl_cascade_tree_plan(const ckl_decode_params* base, const int* h_indptr,
+                                         const int* h_indices, const int* h_lens,
+                                         int min_prefix, ckl_cascade_tree_plan_t* plan,
+                                         void* tables, size_t table_bytes);
+
+CKL_API size_t ckl_cascade_tree_workspace_size(const ckl_cascade_tree_plan_t* plan);
+
+/* Prefix kernel over every node's work items, the suffix partial kernel from each
+ * sequence's own start, and one LSE merge of each sequence's own slots. d_tables is the
+ * plan's tables in device memory. Results equal ckl_decode_attention's up to the fp32
+ * summation order of the split. */
+CKL_API ckl_status ckl_cascade_tree_decode(const ckl_cascade_tree_plan_t* plan,
+                                           const void* d_tables, void* out, float* lse,
+                                           void* workspace, size_t workspace_bytes,
+                                           void* stream);
+
 /* ======================================================================================
  * Weight-only quantised MoE decode layer (W4A16 / W8A16 / fp16 experts)
  * ==================================================================================== */

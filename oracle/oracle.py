@@ -148,6 +148,76 @@ def shared_prefix_pages(indptr, indices):
 
 
 # ------------------------------------------------------------------ MoE
+def prefix_tree_batch(segments, seqs, Hq, Hkv, seed, fill=True):
+    """A paged batch whose sequences share runs of physical pages (a prefix tree).
+
+    No reference generator exists for it (the reference lists prefix trees as not done,
+    README.md:73); this follows make_shared_prefix_batch (01:446-484) in spirit: segment i
+    is segments[i] pages stored once, sequence b = its segment list seqs[b][0] followed by
+    seqs[b][1] >= 1 private tokens, physical page ids shuffled, K/V/q U(-1,1) fp16 from a
+    numpy generator seeded with `seed`."""
+    rng = np.random.default_rng(seed)
+    seg_base, n = [], 0
+    for pages in segments:
+        seg_base.append(n)
+        n += pages
+    lists, lens, last = [], [], []
+    for segs, priv in seqs:
+        assert priv >= 1
+        pl = [seg_base[i] + j for i in segs for j in range(segments[i])]
+        npriv = (priv + PAGE - 1) // PAGE
+        pl += list(range(n, n + npriv))
+        n += npriv
+        lists.append(pl)
+        lens.append(PAGE * sum(segments[i] for i in segs) + priv)
+        last.append(priv - (npriv - 1) * PAGE)
+    phys = rng.permutation(n).astype(np.int32)
+    indptr = np.zeros(len(seqs) + 1, np.int32)
+    indptr[1:] = np.cumsum([len(pl) for pl in lists])
+    indices = np.array([phys[i] for pl in lists for i in pl], np.int32)
+    q = (rng.random((len(seqs), Hq, HEAD_DIM), np.float32) * 2 - 1).astype(np.float16)
+    k = v = None
+    if fill:
+        k = (rng.random((n, PAGE, Hkv, HEAD_DIM), np.float32) * 2 - 1).astype(np.float16)
+        v = (rng.random((n, PAGE, Hkv, HEAD_DIM), np.float32) * 2 - 1).astype(np.float16)
+    bt = Batch(lens, Hq, Hkv, indptr, indices, np.array(last, np.int32), q, k, v)
+    bt.num_pages = n
+    return bt
+
+
+def prefix_tree_ref(indptr, indices, min_pages=1):
+    """Brute-force prefix tree of a page table (checker for ckl_prefix_tree).
+
+    Each sequence's key is its page list but the last page. A node is a maximal set of >= 2
+    sequences whose keys share their first `end` pages; taken by increasing depth, a node is
+    kept when end - first >= min_pages, first being the end of its nearest kept ancestor
+    (a kept node whose members strictly include its own). Returns ({(members, first, end)},
+    start_pages[B] = end of each sequence's deepest kept node, else 0)."""
+    ip = np.asarray(indptr)
+    B = len(ip) - 1
+    keys = [tuple(int(x) for x in indices[ip[b]:max(ip[b], ip[b + 1] - 1)]) for b in range(B)]
+    best = {}
+    for depth in range(1, max((len(k) for k in keys), default=0) + 1):
+        groups = {}
+        for b in range(B):
+            if len(keys[b]) >= depth:
+                groups.setdefault(keys[b][:depth], []).append(b)
+        for g in groups.values():
+            if len(g) >= 2:
+                best[frozenset(g)] = depth
+    kept = []
+    for members, end in sorted(best.items(), key=lambda kv: kv[1]):
+        anc = [e for (m, f, e) in kept if members < m]
+        first = max(anc, default=0)
+        if end - first >= max(1, min_pages):
+            kept.append((members, first, end))
+    start = np.zeros(B, np.int32)
+    for members, first, end in kept:
+        for b in members:
+            start[b] = max(start[b], end)
+    return set(kept), start
+
+
 def make_logits(T, E, seed, disable=-1, msvc_pair_order=False):
     """Restates make_logits; msvc_pair_order reproduces the MSVC build that produced the
     reference's published results (see ckl_oracle.cpp)."""

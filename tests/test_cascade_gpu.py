@@ -129,3 +129,103 @@ def test_config3_uniform_suffix_sampled(ckl, oracle, dev):
 def test_config3_ragged_suffix_sampled(ckl, oracle, dev):
     suffix = np.random.default_rng(77).integers(1, 1025, size=64)
     _config3(ckl, oracle, dev, suffix, sample=(0, 17, 63))
+
+
+# ------------------------------------------------------------------ prefix-tree cascade
+def run_tree(ckl, bt, d, min_prefix):
+    base = ckl.make_params(**d, num_chunks=1, chunk_tokens=16)
+    tp = ckl.plan_cascade_tree(base, bt.indptr, bt.indices, bt.lens, min_prefix)
+    out, lse = ckl.cascade_tree_decode(tp)
+    return tp, out, lse
+
+
+# (segments in pages, sequences as (segment list, private tokens), Hq, Hkv): a system
+# prompt under two documents, sequences outside every group, and a second unrelated tree
+TREE_CASES = [
+    ([8, 12, 6, 20],
+     [([0, 1], 40), ([0, 1], 3), ([0, 1], 17), ([0, 2], 100), ([0, 2], 1), ([0], 70), ([], 300),
+      ([3], 16), ([3], 9)], 32, 8),
+    ([4, 16], [([0, 1], 5), ([0, 1], 50), ([0], 33), ([0], 1)], 16, 2),
+    ([30], [([0], 1), ([0], 2), ([0], 700)], 8, 8),
+]
+
+
+@pytest.mark.parametrize("segments,seqs,Hq,Hkv", TREE_CASES)
+def test_tree_cascade_against_oracle(ckl, oracle, dev, segments, seqs, Hq, Hkv):
+    bt = oracle.prefix_tree_batch(segments, seqs, Hq, Hkv, 31)
+    ref_o, ref_l = oracle.attention_ref(bt)
+    tp, out, lse = run_tree(ckl, bt, to_dev(bt, dev), 16)
+    want, _ = oracle.prefix_tree_ref(bt.indptr, bt.indices, 1)
+    assert tp.use == 1 and tp.nodes == len(want)
+    check(out, lse, ref_o, ref_l, f"tree {segments}")
+
+
+def test_tree_cascade_min_prefix_and_fallback(ckl, oracle, dev):
+    segments, seqs, Hq, Hkv = TREE_CASES[0]
+    bt = oracle.prefix_tree_batch(segments, seqs, Hq, Hkv, 32)
+    ref_o, ref_l = oracle.attention_ref(bt)
+    d = to_dev(bt, dev)
+    tp, out, lse = run_tree(ckl, bt, d, 256)        # 16 pages: only the 20-page segment and 0+1
+    assert tp.use == 1 and tp.nodes == 2
+    check(out, lse, ref_o, ref_l, "tree min_prefix 256")
+    tp, out, lse = run_tree(ckl, bt, d, 1 << 20)    # nothing long enough: plain split-KV
+    assert tp.use == 0
+    check(out, lse, ref_o, ref_l, "tree fallback")
+    bt = oracle.batch([1000] * 4, 32, 8, 3)
+    tp, out, lse = run_tree(ckl, bt, to_dev(bt, dev), 16)
+    assert tp.use == 0
+    ref_o, ref_l = oracle.attention_ref(bt)
+    check(out, lse, ref_o, ref_l, "tree unshared")
+
+
+def test_tree_cascade_whole_batch_prefix_matches_cascade(ckl, oracle, dev):
+    bt = oracle.shared_prefix_batch(1024, [77] * 40, 32, 8, 13)
+    d = to_dev(bt, dev)
+    tp, o1, l1 = run_tree(ckl, bt, d, 16)
+    assert tp.use == 1 and tp.nodes == 1
+    _, o2, l2 = run_tree(ckl, bt, d, 16)
+    assert bool((o1 == o2).all()) and bool((l1 == l2).all()), "not deterministic"
+    _, co, cl = run_cascade(ckl, bt, d, 16)
+    assert float((o1.float() - co.float()).abs().max()) <= 2 * OUT_ATOL
+    ref_o, ref_l = oracle.attention_ref(bt)
+    check(o1, l1, ref_o, ref_l, "tree whole-batch prefix")
+
+
+def tree_config(n_groups=4, per_group=16, system=1024, doc=4096, suffix=256):
+    """Config-3-sized prefix tree: a system prompt shared by all sequences, one document per
+    group of sequences, private suffixes (token counts)."""
+    segments = [system // 16] + [doc // 16] * n_groups
+    suffix = np.broadcast_to(np.asarray(suffix), (n_groups * per_group,))
+    seqs = [([0, 1 + g], int(suffix[g * per_group + i]))
+            for g in range(n_groups) for i in range(per_group)]
+    return segments, seqs
+
+
+def test_tree_config_sampled(ckl, oracle, dev):
+    import torch
+    Hq, Hkv = 32, 8
+    segments, seqs = tree_config(suffix=np.random.default_rng(5).integers(1, 1025, size=64))
+    bt = oracle.prefix_tree_batch(segments, seqs, Hq, Hkv, 41, fill=False)
+    g = torch.Generator(device=dev)
+    g.manual_seed(41)
+    shape = (bt.num_pages, 16, Hkv, 128)
+    k = (torch.rand(shape, generator=g, device=dev) * 2 - 1).half()
+    v = (torch.rand(shape, generator=g, device=dev) * 2 - 1).half()
+    q = (torch.rand((bt.B, Hq, 128), generator=g, device=dev) * 2 - 1).half()
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+    d = dict(q=q, k_cache=k, v_cache=v, kv_indptr=t(bt.indptr), kv_indices=t(bt.indices),
+             kv_last_page_len=t(bt.last))
+    tp, out, lse = run_tree(ckl, bt, d, 256)
+    assert tp.use == 1 and tp.nodes == 5
+    po, pl = ckl.decode_attention(**d)
+    assert float((out.float() - po.float()).abs().max()) <= 2 * OUT_ATOL
+    out, lse = out.float().cpu().numpy(), lse.cpu().numpy()
+    for b in (0, 17, 40, 63):
+        pages = bt.indices[bt.indptr[b]:bt.indptr[b + 1]]
+        pi = torch.from_numpy(pages.astype(np.int64)).to(dev)
+        sb = oracle.Batch([bt.lens[b]], Hq, Hkv, np.array([0, len(pages)], np.int32),
+                          np.arange(len(pages), dtype=np.int32), bt.last[b:b + 1],
+                          q[b:b + 1].cpu().numpy(), k.index_select(0, pi).cpu().numpy(),
+                          v.index_select(0, pi).cpu().numpy())
+        ro, rl = oracle.attention_ref(sb)
+        check_np(out[b], lse[b], ro[0], rl[0], f"tree config b={b}")
