@@ -118,6 +118,8 @@ _SIGS = {
                                         C.c_void_p, C.c_int, C.POINTER(CascadeTreePlan),
                                         C.c_void_p, C.c_size_t]),
     "ckl_cascade_tree_workspace_size": (C.c_size_t, [C.POINTER(CascadeTreePlan)]),
+    "ckl_cascade_tree_prefix": (C.c_int, [C.POINTER(CascadeTreePlan), C.c_void_p, C.c_void_p,
+                                          C.c_void_p, C.c_void_p]),
     "ckl_cascade_tree_decode": (C.c_int, [C.POINTER(CascadeTreePlan), C.c_void_p, C.c_void_p,
                                           C.c_void_p, C.c_void_p, C.c_size_t, C.c_void_p]),
     "ckl_cascade_decode": (C.c_int, [C.POINTER(CascadePlan), C.c_void_p, C.c_void_p,
@@ -469,6 +471,11 @@ def plan_cascade_tree(base: DecodeParams, h_indptr, h_indices, h_lens, min_prefi
 
 def cascade_tree_workspace_size(tp: CascadeTreePlan):
     return lib().ckl_cascade_tree_workspace_size(C.byref(tp))
+
+
+def cascade_tree_prefix(tp: CascadeTreePlan, part_o, part_lse, stream=None):
+    check(lib().ckl_cascade_tree_prefix(C.byref(tp), _ptr(tp.tables), _ptr(part_o),
+                                        _ptr(part_lse), _stream(stream)), "ckl_cascade_tree_prefix")
 
 
 def cascade_tree_decode(tp: CascadeTreePlan, out=None, lse=None, workspace=None, stream=None):

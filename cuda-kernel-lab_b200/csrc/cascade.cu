@@ -28,7 +28,7 @@ namespace cascade {
 
 using namespace attn;
 
-constexpr int PWARPS = 8;                     // consumer warps, 16 stacked query rows each
+constexpr int PWARPS = 4;                     // consumer warps, 16 stacked query rows each
 constexpr int PROWS = PWARPS * 16;            // query rows per CTA
 constexpr int PTHREADS = (PWARPS + 1) * 32;   // + one TMA producer warp
 constexpr int PSTAGES = 8;
@@ -56,7 +56,7 @@ struct PrefixArgs {
 // every stacked query row it covers into slot blockIdx.x. Prefix-tree mode: grid = (work
 // items, 1, Hkv); item x covers a run of pages shared by the sequences perm[m0, m0 + members)
 // and its stacked rows [row0, row0 + 128) of members x G, written into the item's slot.
-__global__ void __launch_bounds__(PTHREADS, 1)
+__global__ void __launch_bounds__(PTHREADS, 2)
 cascade_prefix_kernel(const __grid_constant__ CUtensorMap tmK,
                       const __grid_constant__ CUtensorMap tmV, const PrefixArgs a) {
     extern __shared__ uint8_t smem_raw[];
@@ -387,6 +387,22 @@ ckl_status launch_tree_prefix(const ckl_cascade_tree_plan_t* tp, const uint8_t* 
     return CKL_OK;
 }
 
+ckl_status check_tree_plan(const ckl_cascade_tree_plan_t* tp, const void* d_tables, int* G) {
+    if (!tp) return fail(CKL_INVALID_ARG, "cascade tree plan is NULL");
+    if (!tp->use) return fail(CKL_INVALID_ARG, "cascade tree plan has no shared node");
+    const ckl_decode_params& sp = tp->suffix;
+    ckl_status st = attn::validate(&sp, G);
+    if (st != CKL_OK) return st;
+    if (tp->nodes <= 0 || tp->items <= 0 || tp->chunk_pages <= 0 || tp->max_path_slots <= 0 ||
+        sp.kv_start != 0 || sp.chunk_base != 0 || sp.part_stride != tp->max_path_slots + sp.num_chunks ||
+        tp->table_bytes != tree_tables(sp.B, tp->items).bytes)
+        return fail(CKL_INVALID_ARG, "inconsistent cascade tree plan");
+    if (tp->suffix.Hkv > 65535) return fail(CKL_UNSUPPORTED_SHAPE, "cascade grid too large");
+    if (!d_tables || ((uintptr_t)d_tables & 15))
+        return fail(CKL_INVALID_ARG, "cascade tree tables must be 16-byte aligned device memory");
+    return CKL_OK;
+}
+
 }  // namespace cascade
 }  // namespace ckl
 
@@ -666,6 +682,16 @@ size_t ckl_cascade_tree_workspace_size(const ckl_cascade_tree_plan_t* plan) {
     return attn::part_o_bytes(&s) + align_up((size_t)s.B * s.Hq * s.part_stride * sizeof(float), 256);
 }
 
+ckl_status ckl_cascade_tree_prefix(const ckl_cascade_tree_plan_t* plan, const void* d_tables,
+                                   float* part_o, float* part_lse, void* stream) {
+    int G = 0;
+    ckl_status st = check_tree_plan(plan, d_tables, &G);
+    if (st != CKL_OK || plan->suffix.B == 0) return st;
+    if (!part_o || !part_lse) return fail(CKL_INVALID_ARG, "cascade_tree_prefix: NULL partials");
+    return launch_tree_prefix(plan, static_cast<const uint8_t*>(d_tables), part_o, part_lse,
+                              (cudaStream_t)stream);
+}
+
 ckl_status ckl_cascade_tree_decode(const ckl_cascade_tree_plan_t* plan, const void* d_tables,
                                    void* out, float* lse, void* workspace, size_t workspace_bytes,
                                    void* stream) {
@@ -674,15 +700,8 @@ ckl_status ckl_cascade_tree_decode(const ckl_cascade_tree_plan_t* plan, const vo
         return ckl_decode_attention(&plan->suffix, out, lse, workspace, workspace_bytes, stream);
     const ckl_decode_params& sp = plan->suffix;
     int G = 0;
-    ckl_status st = attn::validate(&sp, &G);
+    ckl_status st = check_tree_plan(plan, d_tables, &G);
     if (st != CKL_OK || sp.B == 0) return st;
-    if (plan->nodes <= 0 || plan->items <= 0 || plan->chunk_pages <= 0 || plan->max_path_slots <= 0 ||
-        sp.kv_start != 0 || sp.chunk_base != 0 ||
-        sp.part_stride != plan->max_path_slots + sp.num_chunks ||
-        plan->table_bytes != tree_tables(sp.B, plan->items).bytes)
-        return fail(CKL_INVALID_ARG, "inconsistent cascade tree plan");
-    if (!d_tables || ((uintptr_t)d_tables & 15))
-        return fail(CKL_INVALID_ARG, "cascade_tree_decode: tables must be 16-byte aligned device memory");
     if (!out || !lse) return fail(CKL_INVALID_ARG, "cascade_tree_decode: out/lse are NULL");
     if ((uintptr_t)out & 7) return fail(CKL_INVALID_ARG, "out needs 8-byte alignment");
     const size_t need = ckl_cascade_tree_workspace_size(plan);

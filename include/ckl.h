@@ -254,6 +254,13 @@ CKL_API ckl_status ckl_cascade_tree_plan(const ckl_decode_params* base, const in
 
 CKL_API size_t ckl_cascade_tree_workspace_size(const ckl_cascade_tree_plan_t* plan);
 
+/* The tree's prefix kernel alone: every node's attention for its members' query heads,
+ * written as their prefix slots of part_o / part_lse (plan->suffix.part_stride slots per
+ * row). */
+CKL_API ckl_status ckl_cascade_tree_prefix(const ckl_cascade_tree_plan_t* plan,
+                                           const void* d_tables, float* part_o,
+                                           float* part_lse, void* stream);
+
 /* Prefix kernel over every node's work items, the suffix partial kernel from each
  * sequence's own start, and one LSE merge of each sequence's own slots. d_tables is the
  * plan's tables in device memory. Results equal ckl_decode_attention's up to the fp32
