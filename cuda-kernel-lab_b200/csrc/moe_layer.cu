@@ -164,11 +164,21 @@ __global__ void combine_kernel(const void* __restrict__ Y, const int* __restrict
                                const float* __restrict__ wts, __half* __restrict__ out, int k, int f) {
     pdl_wait();
     const int t = blockIdx.x;
+    // the k (row, weight) pairs first, so the row loads below do not wait on them one by one
+    int pos_j[MAX_K];
+    float w_j[MAX_K];
+#pragma unroll
+    for (int j = 0; j < MAX_K; j++) {
+        pos_j[j] = j < k ? __ldg(inv_perm + t * k + j) : 0;
+        w_j[j] = j < k ? __ldg(wts + t * k + j) : 0.f;
+    }
     for (int c = threadIdx.x; c < f / 8; c += blockDim.x) {
         float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-        for (int j = 0; j < k; j++) {
-            const int pos = __ldg(inv_perm + t * k + j);
-            const float w = __ldg(wts + t * k + j);
+#pragma unroll
+        for (int j = 0; j < MAX_K; j++) {
+            if (j >= k) break;
+            const int pos = pos_j[j];
+            const float w = w_j[j];
             if (F32) {
                 const float4* src = reinterpret_cast<const float4*>(static_cast<const float*>(Y) + (size_t)pos * f) + 2 * c;
                 const float4 v0 = __ldg(src), v1 = __ldg(src + 1);
