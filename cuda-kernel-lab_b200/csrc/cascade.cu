@@ -7,11 +7,11 @@
 //
 //   1. host: the longest run of physical pages every sequence starts with (each keeps >= 1
 //      private page), from the caller's host copy of the page table;
-//   2. prefix kernel: the B*G query rows that share a kv head are stacked into 128-row tiles
-//      (8 consumer warps x 16 rows); a producer warp TMA-loads each shared page once into an
-//      8-stage ring and every consumer warp runs Q K^T and P V on it with mma.sync, with a
-//      single-pass online softmax (the reference makes two passes because WMMA cannot
-//      rescale its accumulators; register fragments can);
+//   2. prefix kernel: the B*G query rows that share a kv head are stacked into 128-row
+//      tiles, the M of tcgen05.mma: a TMA producer streams the shared pages in 64-key blocks,
+//      S = Q K^T and O += P V run on the tensor cores with S and O in tensor memory, and
+//      eight softmax warps keep a single-pass online softmax (the reference makes two passes
+//      because WMMA cannot rescale its accumulators; O in tensor memory can be);
 //   3. suffix: the split-KV partial kernel from kv_start = prefix length;
 //   4. one LSE merge over prefix and suffix slots.
 
@@ -28,12 +28,40 @@ namespace cascade {
 
 using namespace attn;
 
-constexpr int PWARPS = 4;                     // consumer warps, 16 stacked query rows each
-constexpr int PROWS = PWARPS * 16;            // query rows per CTA
-constexpr int PTHREADS = (PWARPS + 1) * 32;   // + one TMA producer warp
-constexpr int PSTAGES = 8;
-constexpr int P_RING = PSTAGES * STAGE_BYTES;
-constexpr int P_SMEM = 1024 + P_RING + 2 * PSTAGES * 8;
+// The prefix kernel on the 5th-generation tensor cores. A CTA owns PROWS = 128 stacked
+// query rows of one kv head (the M of tcgen05.mma) and streams a run of shared pages in
+// blocks of BLK_PAGES pages (64 keys):
+//   S = Q K^T   M=128, N=64, K=128: Q (K-major) and the block's K rows (K-major) in shared
+//               memory, S in tensor memory (two buffers, so block j+1's S overlaps block j's
+//               softmax);
+//   softmax     4 warps, one thread per row: S row from tensor memory, the online max /
+//               sum in registers (no shuffles), P = exp2(S - m) as fp16 into shared memory
+//               in the K-major swizzled layout of an MMA A operand;
+//   O += P V    M=128, N=128, K=16 per page: P (K-major) and V (MN-major: dims contiguous)
+//               in shared memory, O in tensor memory for the whole run.
+// The running max moves lazily (only when a score exceeds it by 2^RESCALE_THRESHOLD); a
+// move rescales the row's O in tensor memory after the previous P V has landed.
+// Warp 0 lane 0 issues the TMA loads, warp 1 lane 0 the MMAs, warps 2-9 run the softmax:
+// two threads per row (warps 2-5 keys 0-31 of a block and O dims 0-63, warps 6-9 the other
+// halves), which share the row max through shared memory once per block.
+constexpr int PROWS = 128;                    // stacked query rows per CTA (tcgen05 M)
+constexpr int BLK_PAGES = 4;                  // pages per key block
+constexpr int BLK_KEYS = BLK_PAGES * PAGE;    // 64 keys: the N of S = Q K^T
+constexpr int SOFT = 256;                     // softmax threads: 2 per row
+constexpr int PTHREADS = 64 + SOFT;
+constexpr int PSTAGES = 4;                    // key blocks in flight (128 KB)
+constexpr int KV_HALF = BLK_KEYS * 128;       // 64 keys x 64 dims fp16 = 8 KB
+constexpr int BLK_BYTES = 4 * KV_HALF;        // K dims 0-63, K 64-127, V 0-63, V 64-127
+constexpr int Q_BYTES = PROWS * D * 2;        // 32 KB: dims 0-63 then 64-127
+constexpr int P_BYTES = PROWS * BLK_KEYS * 2; // 16 KB per buffer
+constexpr int P_OFF_Q = 0;
+constexpr int P_OFF_RING = Q_BYTES;
+constexpr int P_OFF_P = P_OFF_RING + PSTAGES * BLK_BYTES;
+constexpr int P_OFF_RED = P_OFF_P + 2 * P_BYTES;   // [max parity 0, 1; sums][2 halves][128 rows]
+constexpr int P_OFF_BAR = P_OFF_RED + 3 * 2 * PROWS * 4;
+constexpr int P_NBAR = 2 * PSTAGES + 4 * 2 + 3;
+constexpr int P_SMEM = 1024 + P_OFF_BAR + P_NBAR * 8 + 16;
+constexpr uint32_t P_TMEM_COLS = 256;         // S buffers at columns 0 and 64, O at 128
 
 struct PrefixArgs {
     const __half* q;
@@ -48,21 +76,39 @@ struct PrefixArgs {
     float* part_lse;
     unsigned* err;
     unsigned long long timeout_ns;
-    int B, Hq, Hkv, G, prefix_len, chunk_tokens, part_stride;
+    int B, Hq, Hkv, G, prefix_len, chunk_tokens, part_stride, num_pages;
     float scale_log2;
 };
+
+// Byte offset of 16-byte chunk c (dims/keys 8c..8c+7 of a 128-byte row) of row r in a
+// K-major, 128-byte-swizzled operand whose rows are 128 bytes apart (1024-byte aligned).
+__device__ __forceinline__ uint32_t sw128(int r, int c) {
+    return (uint32_t)(r * 128 + ((c ^ (r & 7)) << 4));
+}
 
 // grid = (prefix chunks, ceil(B*G / 128), Hkv). Writes the normalised partial (o, lse) of
 // every stacked query row it covers into slot blockIdx.x. Prefix-tree mode: grid = (work
 // items, 1, Hkv); item x covers a run of pages shared by the sequences perm[m0, m0 + members)
 // and its stacked rows [row0, row0 + 128) of members x G, written into the item's slot.
-__global__ void __launch_bounds__(PTHREADS, 2)
+__global__ void __launch_bounds__(PTHREADS, 1)
 cascade_prefix_kernel(const __grid_constant__ CUtensorMap tmK,
                       const __grid_constant__ CUtensorMap tmV, const PrefixArgs a) {
     extern __shared__ uint8_t smem_raw[];
-    uint8_t* ring = align_ptr<1024>(smem_raw);
-    uint64_t* full = reinterpret_cast<uint64_t*>(ring + P_RING);
+    uint8_t* sm = align_ptr<1024>(smem_raw);
+    uint8_t* qs = sm + P_OFF_Q;
+    uint8_t* ring = sm + P_OFF_RING;
+    uint8_t* ps = sm + P_OFF_P;
+    float* red = reinterpret_cast<float*>(sm + P_OFF_RED);
+    uint64_t* full = reinterpret_cast<uint64_t*>(sm + P_OFF_BAR);
     uint64_t* empty = full + PSTAGES;
+    uint64_t* s_full = empty + PSTAGES;       // S buffer b written (MMA -> softmax)
+    uint64_t* s_empty = s_full + 2;           // S buffer b read (softmax -> MMA)
+    uint64_t* p_full = s_empty + 2;           // P buffer b written (softmax -> MMA)
+    uint64_t* p_empty = p_full + 2;           // P buffer b consumed (MMA -> softmax)
+    uint64_t* o_done = p_empty + 2;           // one phase per P V block
+    uint64_t* q_full = o_done + 1;            // Q staged (softmax -> MMA)
+    uint64_t* done = q_full + 1;              // every issued MMA finished
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
 
     const int kvh = blockIdx.z;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -89,20 +135,37 @@ cascade_prefix_kernel(const __grid_constant__ CUtensorMap tmK,
         row0 = blockIdx.y * PROWS;
         slot = blockIdx.x;
     }
+    const int nblk = (npg + BLK_PAGES - 1) / BLK_PAGES;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < PSTAGES; s++) {
             mbar_init(&full[s], 1);
-            mbar_init(&empty[s], PWARPS);
+            mbar_init(&empty[s], 1);
         }
+        for (int b = 0; b < 2; b++) {
+            mbar_init(&s_full[b], 1);
+            mbar_init(&s_empty[b], SOFT);
+            mbar_init(&p_full[b], SOFT);
+            mbar_init(&p_empty[b], 1);
+        }
+        mbar_init(o_done, 1);
+        mbar_init(q_full, SOFT);
+        mbar_init(done, 1);
         fence_barrier_init();
     }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, P_TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before_sync();
     __syncthreads();
+    tc_fence_after_sync();
+    const uint32_t tmem = *tmem_slot;
     const uint64_t deadline = globaltimer() + a.timeout_ns;
     pdl_trigger();                   // the suffix kernel (independent slots) may start now
 
-    if (warp == PWARPS) {
-        // ---------------------------------------------------------------- producer warp
+    if (warp == 0) {
+        // ---------------------------------------------------------------- TMA producer
         if (lane == 0) {
             tma_prefetch_desc(&tmK);
             tma_prefetch_desc(&tmV);
@@ -110,169 +173,234 @@ cascade_prefix_kernel(const __grid_constant__ CUtensorMap tmK,
         // the prefix is re-read by the other query tiles of this kv head: keep it in L2
         const uint64_t pol = policy_evict_last();
         int ok = 1, issued = 0;
-        for (int base = 0; base < npg && ok; base += 32) {
-            const int cnt = min(32, npg - base);
-            const int my_page = lane < cnt ? __ldg(pages + base + lane) : 0;
-            for (int j = 0; j < cnt; j++) {
-                const int page = __shfl_sync(0xffffffffu, my_page, j);
-                if (lane == 0) {
-                    const int i = base + j, s = i % PSTAGES;
-                    if (i >= PSTAGES) ok = mbar_wait(&empty[s], ((i / PSTAGES) - 1) & 1, deadline, a.err);
-                    if (ok) {
-                        mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
-                        load_page(ring + s * STAGE_BYTES, &tmK, &tmV, kvh, page, &full[s], pol);
-                        issued = i + 1;
-                    }
-                }
-                ok = __shfl_sync(0xffffffffu, ok, 0);
-                if (!ok) break;
+        int ids_at = -32, my_id = 0;     // page ids [ids_at, ids_at + 32): lane l holds one
+        for (int j = 0; j < nblk && ok; j++) {
+            const int s = j % PSTAGES;
+            // the run's page ids, 32 per warp-wide load (one load per 8 blocks, not a
+            // dependent load per block); a page past the run reads as zeros (its coordinate
+            // is past the tensor map's page extent)
+            const int p0 = j * BLK_PAGES;
+            if (p0 >= ids_at + 32) {
+                ids_at = p0 & ~31;
+                my_id = ids_at + lane < npg ? __ldg(pages + ids_at + lane) : a.num_pages;
             }
+            const int my_page = __shfl_sync(0xffffffffu, my_id, (p0 & 31) + (lane & (BLK_PAGES - 1)));
+            if (lane == 0) {
+                if (j >= PSTAGES) ok = mbar_wait(&empty[s], ((j / PSTAGES) - 1) & 1, deadline, a.err);
+                if (ok) mbar_arrive_expect_tx(&full[s], BLK_BYTES);
+            }
+            ok = __shfl_sync(0xffffffffu, ok, 0);
+            if (!ok) break;
+            uint8_t* st = ring + (size_t)s * BLK_BYTES;
+            if (lane < BLK_PAGES) {
+                uint8_t* dst = st + lane * (PAGE * 128);
+                tma_load_4d(dst, &tmK, 0, kvh, 0, my_page, &full[s], pol);
+                tma_load_4d(dst + KV_HALF, &tmK, 64, kvh, 0, my_page, &full[s], pol);
+                tma_load_4d(dst + 2 * KV_HALF, &tmV, 0, kvh, 0, my_page, &full[s], pol);
+                tma_load_4d(dst + 3 * KV_HALF, &tmV, 64, kvh, 0, my_page, &full[s], pol);
+            }
+            issued = j + 1;
         }
-        if (lane == 0) {
+        // every issued copy must land before the CTA exits
+        if (lane == 0)
             for (int s = 0; s < PSTAGES && s < issued; s++) {
-                const int i_last = s + ((issued - 1 - s) / PSTAGES) * PSTAGES;
-                mbar_wait(&full[s], (i_last / PSTAGES) & 1, deadline, a.err);
+                const int last = s + ((issued - 1 - s) / PSTAGES) * PSTAGES;
+                mbar_wait(&full[s], (last / PSTAGES) & 1, deadline, a.err);
             }
-        }
-        return;
-    }
-
-    // -------------------------------------------------------------------- consumer warps
-    const int g = lane >> 2, t = lane & 3;
-    const int r_lo = row0 + warp * 16 + g, r_hi = r_lo + 8;
-    const bool ok_lo = r_lo < nq, ok_hi = r_hi < nq;
-    const bool active = row0 + warp * 16 < nq;   // warp-uniform
-    size_t qrow_lo = 0, qrow_hi = 0;
-    if (ok_lo) {
-        const int seq = a.perm ? __ldg(a.perm + m0 + r_lo / a.G) : r_lo / a.G;
-        qrow_lo = (size_t)seq * a.Hq + (size_t)kvh * a.G + r_lo % a.G;
-    }
-    if (ok_hi) {
-        const int seq = a.perm ? __ldg(a.perm + m0 + r_hi / a.G) : r_hi / a.G;
-        qrow_hi = (size_t)seq * a.Hq + (size_t)kvh * a.G + r_hi % a.G;
-    }
-
-    uint32_t qa0[8], qa1[8], qa2[8], qa3[8];
+    } else if (warp == 1) {
+        // ---------------------------------------------------------------- MMA issuer
+        if (lane == 0) {
+            const uint32_t idesc_s = umma_idesc_f16(PROWS, BLK_KEYS, false, false);
+            const uint32_t idesc_o = umma_idesc_f16(PROWS, D, false, true);
+            const uint32_t qa = smem_u32(qs), pa = smem_u32(ps), ra = smem_u32(ring);
+            bool ok = mbar_wait(q_full, 0, deadline, a.err);
+            // O += P V of block i: one K=16 MMA per page. V is MN-major: its 64-dim atoms
+            // (dims 0-63, 64-127) KV_HALF apart, 8-key groups 1 KB apart.
+            auto pv = [&](int i) {
+                const int s = i % PSTAGES, b = i & 1;
+                if (!mbar_wait(&p_full[b], (i >> 1) & 1, deadline, a.err)) return false;
+                tc_fence_after_sync();
+                const uint32_t vb = ra + (uint32_t)(s * BLK_BYTES + 2 * KV_HALF);
 #pragma unroll
-    for (int kk = 0; kk < 8; kk++) qa0[kk] = qa1[kk] = qa2[kk] = qa3[kk] = 0u;
-    if (ok_lo) {
-        const uint32_t* qr = reinterpret_cast<const uint32_t*>(a.q + qrow_lo * D);
-#pragma unroll
-        for (int kk = 0; kk < 8; kk++) {
-            qa0[kk] = __ldg(qr + 8 * kk + t);
-            qa2[kk] = __ldg(qr + 8 * kk + 4 + t);
-        }
-    }
-    if (ok_hi) {
-        const uint32_t* qr = reinterpret_cast<const uint32_t*>(a.q + qrow_hi * D);
-#pragma unroll
-        for (int kk = 0; kk < 8; kk++) {
-            qa1[kk] = __ldg(qr + 8 * kk + t);
-            qa3[kk] = __ldg(qr + 8 * kk + 4 + t);
-        }
-    }
-    float o[16][4];
-#pragma unroll
-    for (int j = 0; j < 16; j++) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
-    float m_lo = -INFINITY, m_hi = -INFINITY, l_lo = 0.f, l_hi = 0.f;
-    const int k_key = (lane & 7) + ((lane >> 4) << 3), k_hi = (lane >> 3) & 1;
-    const int v_key = (lane & 7) + (((lane >> 3) & 1) << 3), v_hi = lane >> 4;
-
-    bool ok = true;
-    for (int i = 0; i < npg; i++) {
-        const int s = i % PSTAGES;
-        const bool got = mbar_wait(&full[s], (i / PSTAGES) & 1, deadline, a.err);
-        if (!__all_sync(0xffffffffu, got)) { ok = false; break; }
-        if (active) {
-            const uint32_t kb = smem_u32(ring + s * STAGE_BYTES);
-            const uint32_t vb = kb + KV_TILE;
-            float sc[2][4];
-#pragma unroll
-            for (int n = 0; n < 2; n++) sc[n][0] = sc[n][1] = sc[n][2] = sc[n][3] = 0.f;
-#pragma unroll
-            for (int kk = 0; kk < 8; kk++) {
-                uint32_t b00, b01, b10, b11;
-                ldmatrix_x4(kb + tile_off(k_key, 2 * kk + k_hi), b00, b01, b10, b11);
-                mma_16816(sc[0], qa0[kk], qa1[kk], qa2[kk], qa3[kk], b00, b01);
-                mma_16816(sc[1], qa0[kk], qa1[kk], qa2[kk], qa3[kk], b10, b11);
-            }
-            const int kbase = i * PAGE;
-            if (kbase + PAGE > kend) {
-#pragma unroll
-                for (int n = 0; n < 2; n++)
-#pragma unroll
-                    for (int c = 0; c < 4; c++)
-                        if (kbase + n * 8 + 2 * t + (c & 1) >= kend) sc[n][c] = -INFINITY;
-            }
-#pragma unroll
-            for (int n = 0; n < 2; n++)
-#pragma unroll
-                for (int c = 0; c < 4; c++) sc[n][c] *= a.scale_log2;
-            float mx_lo = fmaxf(fmaxf(sc[0][0], sc[0][1]), fmaxf(sc[1][0], sc[1][1]));
-            float mx_hi = fmaxf(fmaxf(sc[0][2], sc[0][3]), fmaxf(sc[1][2], sc[1][3]));
-            mx_lo = fmaxf(mx_lo, __shfl_xor_sync(0xffffffffu, mx_lo, 1));
-            mx_hi = fmaxf(mx_hi, __shfl_xor_sync(0xffffffffu, mx_hi, 1));
-            mx_lo = fmaxf(mx_lo, __shfl_xor_sync(0xffffffffu, mx_lo, 2));
-            mx_hi = fmaxf(mx_hi, __shfl_xor_sync(0xffffffffu, mx_hi, 2));
-            const bool need = mx_lo > m_lo + RESCALE_THRESHOLD || mx_hi > m_hi + RESCALE_THRESHOLD;
-            if (__any_sync(0xffffffffu, need)) {
-                const float mn_lo = fmaxf(m_lo, mx_lo), mn_hi = fmaxf(m_hi, mx_hi);
-                const float c_lo = ex2(m_lo - mn_lo), c_hi = ex2(m_hi - mn_hi);
-                m_lo = mn_lo;
-                m_hi = mn_hi;
-                l_lo *= c_lo;
-                l_hi *= c_hi;
-#pragma unroll
-                for (int j = 0; j < 16; j++) {
-                    o[j][0] *= c_lo;
-                    o[j][1] *= c_lo;
-                    o[j][2] *= c_hi;
-                    o[j][3] *= c_hi;
+                for (int pg = 0; pg < BLK_PAGES; pg++) {
+                    const uint64_t ad = umma_desc_sw128(pa + b * P_BYTES + pg * 32, 16, 1024);
+                    const uint64_t bd = umma_desc_sw128(vb + pg * (PAGE * 128), KV_HALF, 1024);
+                    umma_f16(tmem + 128, ad, bd, idesc_o, (i | pg) != 0);
                 }
-            }
-            const float p00 = ex2(sc[0][0] - m_lo), p01 = ex2(sc[0][1] - m_lo);
-            const float p10 = ex2(sc[1][0] - m_lo), p11 = ex2(sc[1][1] - m_lo);
-            const float q00 = ex2(sc[0][2] - m_hi), q01 = ex2(sc[0][3] - m_hi);
-            const float q10 = ex2(sc[1][2] - m_hi), q11 = ex2(sc[1][3] - m_hi);
-            l_lo += (p00 + p01) + (p10 + p11);
-            l_hi += (q00 + q01) + (q10 + q11);
-            const uint32_t pa0 = pack_half2(p00, p01), pa2 = pack_half2(p10, p11);
-            const uint32_t pa1 = pack_half2(q00, q01), pa3 = pack_half2(q10, q11);
+                umma_commit(&empty[s]);      // K/V block free
+                umma_commit(&p_empty[b]);    // P buffer free
+                umma_commit(o_done);         // O holds blocks 0..i
+                return true;
+            };
+            if (ok) tc_fence_after_sync();
+            for (int j = 0; j < nblk && ok; j++) {
+                const int s = j % PSTAGES, b = j & 1;
+                ok = mbar_wait(&full[s], (j / PSTAGES) & 1, deadline, a.err);
+                if (ok && j >= 2) ok = mbar_wait(&s_empty[b], ((j >> 1) - 1) & 1, deadline, a.err);
+                if (!ok) break;
+                tc_fence_after_sync();
+                const uint32_t kb = ra + (uint32_t)(s * BLK_BYTES);
 #pragma unroll
-            for (int jj = 0; jj < 8; jj++) {
-                uint32_t v0, v1, v2, v3;
-                ldmatrix_x4_trans(vb + tile_off(v_key, 2 * jj + v_hi), v0, v1, v2, v3);
-                mma_16816(o[2 * jj], pa0, pa1, pa2, pa3, v0, v1);
-                mma_16816(o[2 * jj + 1], pa0, pa1, pa2, pa3, v2, v3);
+                for (int kk = 0; kk < 8; kk++) {
+                    // k step of 16 dims = 32 bytes inside the swizzled row; dims 64-127 in the
+                    // second half (Q: 16 KB on, K: KV_HALF on)
+                    const uint64_t ad = umma_desc_sw128(qa + (kk >> 2) * (Q_BYTES / 2) + (kk & 3) * 32, 16, 1024);
+                    const uint64_t bd = umma_desc_sw128(kb + (kk >> 2) * KV_HALF + (kk & 3) * 32, 16, 1024);
+                    umma_f16(tmem + b * BLK_KEYS, ad, bd, idesc_s, kk != 0);
+                }
+                umma_commit(&s_full[b]);
+                if (j >= 1) ok = pv(j - 1);
             }
+            if (ok && nblk > 0) pv(nblk - 1);
+            umma_commit(done);
         }
         __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[s]);
-    }
-    if (!active) return;
+    } else {
+        // ---------------------------------------------------------------- softmax warps
+        const int quarter = warp & 3;                      // TMEM lanes 32*quarter..+31
+        const int hf = (warp - 2) >> 2;                    // which half of the row
+        const int r = quarter * 32 + lane;                 // this thread's row of the tile
+        const uint32_t trow = tmem + ((uint32_t)(quarter * 32) << 16);
+        const int rr = row0 + r;                           // stacked row within the run's rows
+        const bool real = rr < nq;
+        size_t qrow = 0;
+        if (real) {
+            const int seq = a.perm ? __ldg(a.perm + m0 + rr / a.G) : rr / a.G;
+            qrow = (size_t)seq * a.Hq + (size_t)kvh * a.G + rr % a.G;
+        }
+        // stage this thread's half of the q row (zeros past the rows in use) in the swizzled
+        // K-major layout
+        {
+            const uint4* src = reinterpret_cast<const uint4*>(a.q + qrow * D) + 8 * hf;
+#pragma unroll
+            for (int c = 0; c < 8; c++) {
+                const uint4 v = real ? __ldg(src + c) : make_uint4(0u, 0u, 0u, 0u);
+                *reinterpret_cast<uint4*>(qs + hf * (Q_BYTES / 2) + sw128(r, c)) = v;
+            }
+        }
+        fence_proxy_async_smem();                          // visible to the tensor core
+        mbar_arrive(q_full);
 
-    l_lo += __shfl_xor_sync(0xffffffffu, l_lo, 1);
-    l_lo += __shfl_xor_sync(0xffffffffu, l_lo, 2);
-    l_hi += __shfl_xor_sync(0xffffffffu, l_hi, 1);
-    l_hi += __shfl_xor_sync(0xffffffffu, l_hi, 2);
-    if (!ok) { l_lo = l_hi = 0.f; }
-    const float inv_lo = l_lo > 0.f ? 1.f / l_lo : 0.f, inv_hi = l_hi > 0.f ? 1.f / l_hi : 0.f;
-    if (ok_lo) {
-        const size_t pslot = qrow_lo * a.part_stride + slot;
-        float* dst = a.part_o + pslot * D + 2 * t;
+        constexpr int HK = BLK_KEYS / 2;                   // keys of a block per thread
+        float m = -INFINITY, l = 0.f;                      // l: this half's sum
+        // ok is warp-uniform. After a timeout a warp keeps going round the loop without
+        // waiting or computing, so that every softmax thread meets the named barrier the same
+        // number of times (nblk + 1).
+        bool ok = true;
+        for (int j = 0; j < nblk; j++) {
+            const int b = j & 1;
+            if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&s_full[b], (j >> 1) & 1, deadline, a.err));
+            float sv[HK];
+            float mx = -INFINITY;
+            if (ok) {
+                tc_fence_after_sync();
+                uint32_t v[32];
+                tmem_ld32(trow + b * BLK_KEYS + hf * HK, v);
+                tmem_ld_wait();
 #pragma unroll
-        for (int j = 0; j < 16; j++)
-            *reinterpret_cast<float2*>(dst + 8 * j) = make_float2(o[j][0] * inv_lo, o[j][1] * inv_lo);
-        if (t == 0) a.part_lse[pslot] = l_lo > 0.f ? (m_lo + lg2(l_lo)) * LN2 : -INFINITY;
-    }
-    if (ok_hi) {
-        const size_t pslot = qrow_hi * a.part_stride + slot;
-        float* dst = a.part_o + pslot * D + 2 * t;
+                for (int i = 0; i < HK; i++) sv[i] = __uint_as_float(v[i]);
+                tc_fence_before_sync();
+                mbar_arrive(&s_empty[b]);
+                const int kbase = j * BLK_KEYS + hf * HK;
+                if (kbase + HK > kend) {
 #pragma unroll
-        for (int j = 0; j < 16; j++)
-            *reinterpret_cast<float2*>(dst + 8 * j) = make_float2(o[j][2] * inv_hi, o[j][3] * inv_hi);
-        if (t == 0) a.part_lse[pslot] = l_hi > 0.f ? (m_hi + lg2(l_hi)) * LN2 : -INFINITY;
+                    for (int c = 0; c < HK; c++)
+                        if (kbase + c >= kend) sv[c] = -INFINITY;
+                }
+#pragma unroll
+                for (int c = 0; c < HK; c++) mx = fmaxf(mx, sv[c]);
+                mx *= a.scale_log2;                        // scale > 0: max of the scaled row
+            }
+            // the row max across both halves
+            float* rm = red + b * 2 * PROWS;
+            rm[hf * PROWS + r] = mx;
+            asm volatile("bar.sync 1, %0;" ::"n"(SOFT) : "memory");
+            mx = fmaxf(mx, rm[(hf ^ 1) * PROWS + r]);
+            if (!ok) continue;
+            const bool need = mx > m + RESCALE_THRESHOLD;
+            if (__any_sync(0xffffffffu, need)) {
+                const float mn = need ? fmaxf(m, mx) : m;
+                const float cf = ex2(m - mn);              // 0 when m = -inf, 1 when unchanged
+                if (j > 0) {
+                    // O holds blocks 0..j-1 once their P V has landed: rescale this half there
+                    ok = __all_sync(0xffffffffu, mbar_wait(o_done, (j - 1) & 1, deadline, a.err));
+                    if (!ok) continue;
+                    tc_fence_after_sync();
+#pragma unroll
+                    for (int c0 = 0; c0 < D / 2; c0 += 32) {
+                        uint32_t v[32];
+                        tmem_ld32(trow + 128 + hf * (D / 2) + c0, v);
+                        tmem_ld_wait();
+#pragma unroll
+                        for (int i = 0; i < 32; i++) v[i] = __float_as_uint(__uint_as_float(v[i]) * cf);
+                        tmem_st32(trow + 128 + hf * (D / 2) + c0, v);
+                    }
+                    tmem_st_wait();
+                    tc_fence_before_sync();
+                }
+                l *= cf;
+                m = mn;
+            }
+            // P: fp16 exp2(s * scale - m), 8 keys per 16-byte chunk, swizzled
+            if (j >= 2) {
+                ok = __all_sync(0xffffffffu, mbar_wait(&p_empty[b], ((j >> 1) - 1) & 1, deadline, a.err));
+                if (!ok) continue;
+            }
+            uint8_t* prow = ps + b * P_BYTES;
+            const float nm = -m;
+#pragma unroll
+            for (int c = 0; c < HK / 8; c++) {
+                uint32_t w[4];
+#pragma unroll
+                for (int h = 0; h < 4; h++) {
+                    const float p0 = ex2(fmaf(sv[8 * c + 2 * h], a.scale_log2, nm));
+                    const float p1 = ex2(fmaf(sv[8 * c + 2 * h + 1], a.scale_log2, nm));
+                    l += p0 + p1;
+                    w[h] = pack_half2(p0, p1);
+                }
+                *reinterpret_cast<uint4*>(prow + sw128(r, hf * (HK / 8) + c)) = make_uint4(w[0], w[1], w[2], w[3]);
+            }
+            fence_proxy_async_smem();
+            mbar_arrive(&p_full[b]);
+        }
+        // epilogue: this half of the O row / l, and the lse, into the partial slot
+        if (ok && nblk > 0) ok = __all_sync(0xffffffffu, mbar_wait(o_done, (nblk - 1) & 1, deadline, a.err));
+        const bool good = ok && nblk > 0;
+        // the sums of the two halves (every softmax thread reaches this barrier once)
+        float* rl = red + 4 * PROWS;
+        rl[hf * PROWS + r] = l;
+        asm volatile("bar.sync 1, %0;" ::"n"(SOFT) : "memory");
+        l += rl[(hf ^ 1) * PROWS + r];
+        if (good) {
+            tc_fence_after_sync();
+            const float inv = l > 0.f ? 1.f / l : 0.f;
+            const size_t pslot = qrow * a.part_stride + slot;
+            float4* dst = reinterpret_cast<float4*>(a.part_o + pslot * D + hf * (D / 2));
+#pragma unroll
+            for (int c0 = 0; c0 < D / 2; c0 += 32) {
+                uint32_t v[32];
+                tmem_ld32(trow + 128 + hf * (D / 2) + c0, v);
+                tmem_ld_wait();
+                if (real) {
+#pragma unroll
+                    for (int i = 0; i < 32; i += 4)
+                        dst[(c0 + i) / 4] = make_float4(__uint_as_float(v[i]) * inv, __uint_as_float(v[i + 1]) * inv,
+                                                        __uint_as_float(v[i + 2]) * inv, __uint_as_float(v[i + 3]) * inv);
+                }
+            }
+            if (real && hf == 0) a.part_lse[pslot] = l > 0.f ? (m + lg2(l)) * LN2 : -INFINITY;
+        } else if (nblk == 0 && real) {                    // an empty run: no keys
+            const size_t pslot = qrow * a.part_stride + slot;
+            for (int c = 0; c < D / 2; c++) a.part_o[pslot * D + hf * (D / 2) + c] = 0.f;
+            if (hf == 0) a.part_lse[pslot] = -INFINITY;
+        }
     }
+    // every MMA must have finished before tensor memory is released
+    if (threadIdx.x == 0) mbar_wait(done, 0, deadline, a.err);
+    tc_fence_before_sync();
+    __syncthreads();
+    tc_fence_after_sync();
+    if (warp == 1) tmem_dealloc(tmem, P_TMEM_COLS);
 }
 
 struct PrefixSetup {
@@ -317,6 +445,7 @@ ckl_status launch_prefix(const ckl_cascade_plan_t* cp, float* part_o, float* par
     a.prefix_len = cp->prefix_len;
     a.chunk_tokens = cp->prefix_chunk_tokens;
     a.part_stride = b.part_stride;
+    a.num_pages = b.num_pages;
     a.scale_log2 = b.sm_scale * LOG2E;
     void* args[] = {&tmK, &tmV, &a};
     dim3 grid((unsigned)cp->prefix_chunks, (unsigned)cp->qtiles, (unsigned)b.Hkv);
@@ -379,6 +508,7 @@ ckl_status launch_tree_prefix(const ckl_cascade_tree_plan_t* tp, const uint8_t* 
     a.Hkv = b.Hkv;
     a.G = b.Hq / b.Hkv;
     a.part_stride = b.part_stride;
+    a.num_pages = b.num_pages;
     a.scale_log2 = b.sm_scale * LOG2E;
     void* args[] = {&tmK, &tmV, &a};
     dim3 grid((unsigned)tp->items, 1, (unsigned)b.Hkv);
@@ -611,7 +741,20 @@ ckl_status ckl_cascade_tree_plan(const ckl_decode_params* base, const int* h_ind
         work += (long long)(nd[1] - nd[0]) * ceil_div((nd[3] - nd[2]) * G, PROWS);
     }
     const long long target = std::max(1LL, (long long)di->sms * std::max(1, ps->per_sm) / base->Hkv);
-    const int cp = (int)std::max(16LL, (work + target - 1) / target);
+    // the smallest chunk that keeps every work item in the one wave (a partial second wave
+    // would double the prefix time)
+    auto items_for = [&](int c) {
+        long long it = 0;
+        for (int i = 0; i < n; i++) {
+            const int* nd = &nodes[5 * i];
+            it += (long long)ceil_div(nd[1] - nd[0], c) * ceil_div((nd[3] - nd[2]) * G, PROWS);
+        }
+        return it;
+    };
+    int cp = (int)std::max(16LL, (work + target - 1) / target);
+    int max_run = 1;
+    for (int i = 0; i < n; i++) max_run = std::max(max_run, nodes[5 * i + 1] - nodes[5 * i]);
+    while (cp < max_run && items_for(cp) > target) cp++;
     // slots: a node's chunks follow its kept ancestors' chunks
     std::vector<int> nchunks(n), slot0(n);
     int items = 0;
