@@ -49,15 +49,16 @@ constexpr int BLK_PAGES = 4;                  // pages per key block
 constexpr int BLK_KEYS = BLK_PAGES * PAGE;    // 64 keys: the N of S = Q K^T
 constexpr int SOFT = 256;                     // softmax threads: 2 per row
 constexpr int PTHREADS = 64 + SOFT;
-constexpr int PSTAGES = 4;                    // key blocks in flight (128 KB)
+constexpr int PSTAGES = 5;                    // key blocks in flight (160 KB)
 constexpr int KV_HALF = BLK_KEYS * 128;       // 64 keys x 64 dims fp16 = 8 KB
 constexpr int BLK_BYTES = 4 * KV_HALF;        // K dims 0-63, K 64-127, V 0-63, V 64-127
 constexpr int Q_BYTES = PROWS * D * 2;        // 32 KB: dims 0-63 then 64-127
 constexpr int P_BYTES = PROWS * BLK_KEYS * 2; // 16 KB per buffer
+constexpr int PBUF = 1;                       // P buffers (one: the ring gets the room)
 constexpr int P_OFF_Q = 0;
 constexpr int P_OFF_RING = Q_BYTES;
 constexpr int P_OFF_P = P_OFF_RING + PSTAGES * BLK_BYTES;
-constexpr int P_OFF_RED = P_OFF_P + 2 * P_BYTES;   // [max parity 0, 1; sums][2 halves][128 rows]
+constexpr int P_OFF_RED = P_OFF_P + PBUF * P_BYTES;   // [max parity 0, 1; sums][2 halves][128 rows]
 constexpr int P_OFF_BAR = P_OFF_RED + 3 * 2 * PROWS * 4;
 constexpr int P_NBAR = 2 * PSTAGES + 4 * 2 + 3;
 constexpr int P_SMEM = 1024 + P_OFF_BAR + P_NBAR * 8 + 16;
@@ -103,9 +104,9 @@ cascade_prefix_kernel(const __grid_constant__ CUtensorMap tmK,
     uint64_t* empty = full + PSTAGES;
     uint64_t* s_full = empty + PSTAGES;       // S buffer b written (MMA -> softmax)
     uint64_t* s_empty = s_full + 2;           // S buffer b read (softmax -> MMA)
-    uint64_t* p_full = s_empty + 2;           // P buffer b written (softmax -> MMA)
-    uint64_t* p_empty = p_full + 2;           // P buffer b consumed (MMA -> softmax)
-    uint64_t* o_done = p_empty + 2;           // one phase per P V block
+    uint64_t* p_full = s_empty + 2;           // P buffer written (softmax -> MMA)
+    uint64_t* p_empty = p_full + PBUF;        // P buffer consumed (MMA -> softmax)
+    uint64_t* o_done = p_empty + PBUF;        // one phase per P V block
     uint64_t* q_full = o_done + 1;            // Q staged (softmax -> MMA)
     uint64_t* done = q_full + 1;              // every issued MMA finished
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
@@ -145,6 +146,8 @@ cascade_prefix_kernel(const __grid_constant__ CUtensorMap tmK,
         for (int b = 0; b < 2; b++) {
             mbar_init(&s_full[b], 1);
             mbar_init(&s_empty[b], SOFT);
+        }
+        for (int b = 0; b < PBUF; b++) {
             mbar_init(&p_full[b], SOFT);
             mbar_init(&p_empty[b], 1);
         }
@@ -217,8 +220,8 @@ cascade_prefix_kernel(const __grid_constant__ CUtensorMap tmK,
             // O += P V of block i: one K=16 MMA per page. V is MN-major: its 64-dim atoms
             // (dims 0-63, 64-127) KV_HALF apart, 8-key groups 1 KB apart.
             auto pv = [&](int i) {
-                const int s = i % PSTAGES, b = i & 1;
-                if (!mbar_wait(&p_full[b], (i >> 1) & 1, deadline, a.err)) return false;
+                const int s = i % PSTAGES, b = i % PBUF;
+                if (!mbar_wait(&p_full[b], (i / PBUF) & 1, deadline, a.err)) return false;
                 tc_fence_after_sync();
                 const uint32_t vb = ra + (uint32_t)(s * BLK_BYTES + 2 * KV_HALF);
 #pragma unroll
@@ -342,11 +345,12 @@ cascade_prefix_kernel(const __grid_constant__ CUtensorMap tmK,
                 m = mn;
             }
             // P: fp16 exp2(s * scale - m), 8 keys per 16-byte chunk, swizzled
-            if (j >= 2) {
-                ok = __all_sync(0xffffffffu, mbar_wait(&p_empty[b], ((j >> 1) - 1) & 1, deadline, a.err));
+            const int pb = j % PBUF;
+            if (j >= PBUF) {
+                ok = __all_sync(0xffffffffu, mbar_wait(&p_empty[pb], ((j / PBUF) - 1) & 1, deadline, a.err));
                 if (!ok) continue;
             }
-            uint8_t* prow = ps + b * P_BYTES;
+            uint8_t* prow = ps + pb * P_BYTES;
             const float nm = -m;
 #pragma unroll
             for (int c = 0; c < HK / 8; c++) {
@@ -361,7 +365,7 @@ cascade_prefix_kernel(const __grid_constant__ CUtensorMap tmK,
                 *reinterpret_cast<uint4*>(prow + sw128(r, hf * (HK / 8) + c)) = make_uint4(w[0], w[1], w[2], w[3]);
             }
             fence_proxy_async_smem();
-            mbar_arrive(&p_full[b]);
+            mbar_arrive(&p_full[pb]);
         }
         // epilogue: this half of the O row / l, and the lse, into the partial slot
         if (ok && nblk > 0) ok = __all_sync(0xffffffffu, mbar_wait(o_done, (nblk - 1) & 1, deadline, a.err));
