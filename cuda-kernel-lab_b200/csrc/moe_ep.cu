@@ -35,16 +35,12 @@
 
 #include "ckl_internal.h"
 #include "ckl_ptx.cuh"
+#include "moe_internal.h"
 
 namespace ckl {
 namespace moe {
 
-ckl_status expert_gemm(const void* X, const int* row_src, const int* offsets, int A, int max_rows,
-                       const ckl_moe_weights* w0, const ckl_moe_weights* w1, void* Y, int y_f32,
-                       int force_ksplit, void* workspace, size_t workspace_bytes, void* stream,
-                       int dep, const int* row_dst = nullptr, const int* a_rows = nullptr);
-ckl_status route_tokens(const float* logits, int T, int E, int k, int* ids, float* wts,
-                        int* counts, int* offsets, int* inv_perm, int* row_src, cudaStream_t s);
+
 ckl_status check_route(int T, int E, int k);
 
 constexpr int EP_MAX_E = 256;

@@ -26,6 +26,7 @@
 #include "ckl_internal.h"
 #include "ckl_ptx.cuh"
 #include "moe_common.cuh"
+#include "moe_internal.h"
 
 namespace ckl {
 namespace moe {
@@ -663,14 +664,6 @@ int pick_ksplit(const DeviceInfo* di, int quads, int slots, int K) {
 }  // namespace moe
 }  // namespace ckl
 
-namespace ckl {
-namespace moe {
-ckl_status expert_gemm(const void* X, const int* row_src, const int* offsets, int A, int max_rows,
-                       const ckl_moe_weights* w0, const ckl_moe_weights* w1, void* Y, int y_f32,
-                       int force_ksplit, void* workspace, size_t workspace_bytes, void* stream,
-                       int dep = 0, const int* row_dst = nullptr, const int* a_rows = nullptr);
-}  // namespace moe
-}  // namespace ckl
 
 using namespace ckl;
 using namespace ckl::moe;

@@ -22,14 +22,10 @@
 
 #include "ckl_internal.h"
 #include "ckl_ptx.cuh"
+#include "moe_internal.h"
 
 namespace ckl {
 namespace moe {
-
-ckl_status expert_gemm(const void* X, const int* row_src, const int* offsets, int A, int max_rows,
-                       const ckl_moe_weights* w0, const ckl_moe_weights* w1, void* Y, int y_f32,
-                       int force_ksplit, void* workspace, size_t workspace_bytes, void* stream,
-                       int dep, const int* row_dst = nullptr, const int* a_rows = nullptr);
 
 constexpr int MAX_E = 256;
 constexpr int MAX_K = 8;
