@@ -34,9 +34,9 @@ using namespace attn;
 //   S = Q K^T   M=128, N=64, K=128: Q (K-major) and the block's K rows (K-major) in shared
 //               memory, S in tensor memory (two buffers, so block j+1's S overlaps block j's
 //               softmax);
-//   softmax     4 warps, one thread per row: S row from tensor memory, the online max /
-//               sum in registers (no shuffles), P = exp2(S - m) as fp16 into shared memory
-//               in the K-major swizzled layout of an MMA A operand;
+//   softmax     8 warps, two threads per row: half an S row from tensor memory each, the
+//               online max / sum in registers, P = exp2(S * scale - m) as fp16 into shared
+//               memory in the K-major swizzled layout of an MMA A operand;
 //   O += P V    M=128, N=128, K=16 per page: P (K-major) and V (MN-major: dims contiguous)
 //               in shared memory, O in tensor memory for the whole run.
 // The running max moves lazily (only when a score exceeds it by 2^RESCALE_THRESHOLD); a
