@@ -19,26 +19,43 @@ constexpr float LN2 = 0.6931471805599453f;
 constexpr float RESCALE_THRESHOLD = 8.f;   // log2 units: p may grow to 2^8 before a rescale
 
 // Byte offset of 16-byte chunk `cd` (0..15, dims 8cd..8cd+7) of key `key` inside a page
-// tile: [half = cd/8][key][64 dims] with the TMA 128B swizzle (chunk ^= key%8 within each
-// 128-byte row; the tile is 1024-byte aligned).
+// tile as one page box writes it: 32 rows of 128 bytes, row 2*key + half (half = cd/8, the
+// 64-dim half), with the TMA 128B swizzle (chunk ^= row%8; the tile is 1024-byte aligned).
 __device__ __forceinline__ uint32_t tile_off(int key, int cd) {
-    const int c = cd & 7;
-    return (uint32_t)((cd >> 3) * HALF_TILE + key * 128 + ((c ^ (key & 7)) << 4));
+    const int c = cd & 7, r = 2 * key + (cd >> 3);
+    return (uint32_t)(r * 128 + ((c ^ (r & 7)) << 4));
 }
 
-// Issues the four TMA loads of one page (K and V, dims 0-63 and 64-127) of kv head `kvh`
-// into stage `st`, completing on `bar` (which must expect STAGE_BYTES).
+// Issues the two TMA loads of one page (K and V, all 128 dims) of kv head `kvh` into stage
+// `st`, completing on `bar` (which must expect STAGE_BYTES). Maps of encode_page_maps.
 __device__ __forceinline__ void load_page(uint8_t* st, const CUtensorMap* tmK,
                                           const CUtensorMap* tmV, int kvh, int page,
                                           uint64_t* bar, uint64_t pol) {
-    tma_load_4d(st, tmK, 0, kvh, 0, page, bar, pol);
-    tma_load_4d(st + HALF_TILE, tmK, 64, kvh, 0, page, bar, pol);
-    tma_load_4d(st + KV_TILE, tmV, 0, kvh, 0, page, bar, pol);
-    tma_load_4d(st + KV_TILE + HALF_TILE, tmV, 64, kvh, 0, page, bar, pol);
+    tma_load_5d(st, tmK, 0, 0, kvh, 0, page, bar, pol);
+    tma_load_5d(st + KV_TILE, tmV, 0, 0, kvh, 0, page, bar, pol);
+}
+
+// The K and V caches as the packed 5-D tensors [num_pages][16 tokens][Hkv][2 halves][64 dims]
+// (the 128 dims split in two 128-byte rows for the swizzle), box 64x2x1x16x1: one TMA load
+// brings one head's page, both halves (4 KB), where two 2 KB boxes would take twice the TMA
+// operations -- and TMA operations, not bytes in flight, bound a CTA's page rate.
+inline ckl_status encode_page_maps(const void* k_cache, const void* v_cache, int Hkv,
+                                   int num_pages, CUtensorMap* tmK, CUtensorMap* tmV) {
+    const uint64_t dims[5] = {64, 2, (uint64_t)Hkv, (uint64_t)PAGE, (uint64_t)num_pages};
+    const uint64_t strides[4] = {128, (uint64_t)D * 2, (uint64_t)Hkv * D * 2,
+                                 (uint64_t)PAGE * Hkv * D * 2};
+    const uint32_t box[5] = {64, 2, 1, (uint32_t)PAGE, 1};
+    ckl_status st = encode_tiled(tmK, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 5,
+                                 const_cast<void*>(k_cache), dims, strides, box,
+                                 CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st != CKL_OK) return st;
+    return encode_tiled(tmV, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 5, const_cast<void*>(v_cache), dims,
+                        strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
 // 4-D maps [128 dims, Hkv, 16 tokens, num_pages] over the K and V caches, box 64x1x16x1,
-// 128-byte swizzle.
+// 128-byte swizzle: one 64-dim half of one head's page per load (the cascade prefix kernel,
+// whose tensor-core operands want each half as its own swizzled tile).
 inline ckl_status encode_kv_maps(const void* k_cache, const void* v_cache, int Hkv,
                                  int num_pages, CUtensorMap* tmK, CUtensorMap* tmV) {
     const uint64_t dims[4] = {(uint64_t)D, (uint64_t)Hkv, (uint64_t)PAGE, (uint64_t)num_pages};

@@ -123,6 +123,16 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const void* tmap, int c0,
         "r"(smem_u32(bar)), "l"(policy)
         : "memory");
 }
+// Tiled 5-D tensor load global -> shared, completing on an mbarrier.
+__device__ __forceinline__ void tma_load_5d(void* dst, const void* tmap, int c0, int c1, int c2,
+                                            int c3, int c4, uint64_t* bar, uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.tensor.5d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1, {%2, %3, %4, %5, %6}], [%7], %8;" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(tmap)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4),
+        "r"(smem_u32(bar)), "l"(policy)
+        : "memory");
+}
 // Tiled 2-D tensor load global -> shared (x coordinate first), completing on an mbarrier.
 __device__ __forceinline__ void tma_load_2d(void* dst, const void* tmap, int c0, int c1, uint64_t* bar,
                                             uint64_t policy) {

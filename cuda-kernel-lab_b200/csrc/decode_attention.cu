@@ -336,7 +336,7 @@ ckl_status launch_partial(const ckl_decode_params* p, int G, bool direct, __half
     if (ks->st != CKL_OK) return ks->st;
 
     CUtensorMap tmK, tmV;
-    ckl_status st = encode_kv_maps(p->k_cache, p->v_cache, p->Hkv, p->num_pages, &tmK, &tmV);
+    ckl_status st = encode_page_maps(p->k_cache, p->v_cache, p->Hkv, p->num_pages, &tmK, &tmV);
     if (st != CKL_OK) return st;
 
     Args a;

@@ -450,7 +450,7 @@ ckl_status ckl_decode_attention_balanced(const ckl_decode_params* p, void* out, 
     uint8_t* ws = static_cast<uint8_t*>(workspace);
 
     CUtensorMap tmK, tmV;
-    st = encode_kv_maps(p->k_cache, p->v_cache, p->Hkv, p->num_pages, &tmK, &tmV);
+    st = encode_page_maps(p->k_cache, p->v_cache, p->Hkv, p->num_pages, &tmK, &tmV);
     if (st != CKL_OK) return st;
     BalArgs a;
     a.q = static_cast<const __half*>(p->q);
