@@ -35,6 +35,9 @@ namespace attn {
 constexpr int CONSUMERS = 4;
 constexpr int THREADS = (CONSUMERS + 1) * 32;
 constexpr int STAGES = 8;
+// Consumer warp w takes pages i = w (mod CONSUMERS) from stage i % STAGES: each stage then has
+// one consumer warp, which meets its phases in order (the parity waits rely on it).
+static_assert(STAGES % CONSUMERS == 0, "every stage must belong to one consumer warp");
 constexpr int RING_BYTES = STAGES * STAGE_BYTES;
 constexpr int BAR_BYTES = 2 * STAGES * 8;
 constexpr int RED_BYTES = 2 * CONSUMERS * 16 * 4;

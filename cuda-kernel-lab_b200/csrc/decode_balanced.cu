@@ -45,6 +45,7 @@ namespace attn {
 constexpr int BCONS = 4;                       // consumer warps
 constexpr int BTHREADS = (BCONS + 1) * 32;
 constexpr int BSTAGES = 8;
+static_assert(BSTAGES % BCONS == 0, "every stage must belong to one consumer warp");
 constexpr int BRING = BSTAGES * STAGE_BYTES;
 // ring, mbarriers, per-warp (m, l) [4][16] x 2, per-warp O [4][G][128], flag word
 template <int G>
