@@ -229,3 +229,31 @@ def test_tree_config_sampled(ckl, oracle, dev):
                           v.index_select(0, pi).cpu().numpy())
         ro, rl = oracle.attention_ref(sb)
         check_np(out[b], lse[b], ro[0], rl[0], f"tree config b={b}")
+
+
+def test_tree_prefix_alone_fills_each_members_node_slots(ckl, oracle, dev):
+    """ckl_cascade_tree_prefix alone: every member row gets a finite partial in each of its
+    nodes' chunk slots, and the merge of prefix + suffix slots (cascade_tree_decode) equals
+    the oracle; G = 16 (Hq=32, Hkv=2) stacks 16 rows per sequence."""
+    import torch
+    segments, seqs = [10, 20], [([0, 1], 33), ([0, 1], 2), ([0], 70), ([0], 1), ([], 40)]
+    bt = oracle.prefix_tree_batch(segments, seqs, 32, 2, 9)
+    d = to_dev(bt, dev)
+    base = ckl.make_params(**d, num_chunks=1, chunk_tokens=16)
+    tp = ckl.plan_cascade_tree(base, bt.indptr, bt.indices, bt.lens, 16)
+    assert tp.use == 1 and tp.nodes == 2
+    sp = tp.suffix
+    po = torch.full((sp.B * sp.Hq * sp.part_stride * 128,), float("nan"), device=dev)
+    pl = torch.full((sp.B * sp.Hq * sp.part_stride,), float("nan"), device=dev)
+    ckl.cascade_tree_prefix(tp, po, pl)
+    torch.cuda.synchronize()
+    ckl.check_device_error()
+    pl = pl.view(sp.B, sp.Hq, sp.part_stride).cpu().numpy()
+    want, start = oracle.prefix_tree_ref(bt.indptr, bt.indices, 1)
+    for b in range(sp.B):
+        n_prefix = int(start[b] > 0) + int(start[b] > 10)   # nodes on b's path
+        # a member's prefix slots hold finite lse; the rest stay untouched (NaN)
+        assert np.isfinite(pl[b, :, :1]).all() == (n_prefix > 0), b
+    out, lse = ckl.cascade_tree_decode(tp)
+    ref_o, ref_l = oracle.attention_ref(bt)
+    check(out, lse, ref_o, ref_l, "tree G=16")
