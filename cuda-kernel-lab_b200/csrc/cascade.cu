@@ -565,6 +565,12 @@ ckl_status ckl_cascade_plan(const ckl_decode_params* base, const int* h_indptr,
     if (st != CKL_OK) return st;
     *plan = ckl_cascade_plan_t{};
     plan->suffix = *base;
+    if (base->B == 0) {                      // an empty batch: the decode call is a no-op
+        plan->suffix.num_chunks = plan->suffix.part_stride = 1;
+        plan->suffix.chunk_tokens = 32;
+        plan->suffix.kv_start = plan->suffix.chunk_base = 0;
+        return CKL_OK;
+    }
     int max_len = 0;
     for (int b = 0; b < base->B; b++) max_len = std::max(max_len, h_lens[b]);
     const int pages = ckl_shared_prefix_pages(h_indptr, h_indices, base->B);
@@ -725,6 +731,12 @@ ckl_status ckl_cascade_tree_plan(const ckl_decode_params* base, const int* h_ind
     if (n < 0) return fail(CKL_INVALID_ARG, "cascade_tree_plan: bad page table");
     int max_len = 0;
     for (int b = 0; b < B; b++) max_len = std::max(max_len, h_lens[b]);
+    if (B == 0) {                            // an empty batch: the decode call is a no-op
+        plan->suffix.num_chunks = plan->suffix.part_stride = 1;
+        plan->suffix.chunk_tokens = 32;
+        plan->suffix.kv_start = plan->suffix.chunk_base = 0;
+        return CKL_OK;
+    }
     if (n == 0) {
         plan->use = 0;
         st = ckl_decode_plan(G, B, base->Hkv, max_len, 0, &plan->suffix.num_chunks,

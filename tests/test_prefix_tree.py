@@ -114,3 +114,16 @@ def test_random_forests(ckl, oracle, seed):
 def test_bad_table_is_rejected(ckl):
     with pytest.raises(ckl.CklError):
         ckl.prefix_tree(np.array([0, 3, 2], np.int32), np.arange(3, dtype=np.int32))
+
+
+def test_empty_batch_plans_are_no_ops(ckl):
+    """Both cascade planners accept B = 0 (the decode call is then a no-op) without a GPU."""
+    base = ckl.DecodeParams()
+    base.B, base.Hq, base.Hkv, base.num_pages = 0, 32, 8, 4
+    base.num_chunks, base.chunk_tokens, base.part_stride = 1, 16, 1
+    base.sm_scale = 128 ** -0.5
+    e = np.zeros(0, np.int32)
+    cp = ckl.plan_cascade(base, np.zeros(1, np.int32), e, e)
+    assert cp.use == 0 and cp.suffix.num_chunks == 1 and cp.suffix.part_stride == 1
+    tp = ckl.plan_cascade_tree(base, np.zeros(1, np.int32), e, e)
+    assert tp.use == 0 and tp.tables is None and tp.suffix.num_chunks == 1
