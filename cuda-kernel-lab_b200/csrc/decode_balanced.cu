@@ -46,6 +46,10 @@ constexpr int BCONS = 4;                       // consumer warps
 constexpr int BTHREADS = (BCONS + 1) * 32;
 constexpr int BSTAGES = 8;
 static_assert(BSTAGES % BCONS == 0, "every stage must belong to one consumer warp");
+static_assert(BCONS * 32 == D, "the split-unit merge gives each consumer thread one column");
+// Most head groups per launch: the merge stages a unit's nc <= NG lse rows of G floats in
+// o_red, which holds BCONS * D rows.
+constexpr int BMAX_GROUPS = BCONS * D;
 constexpr int BRING = BSTAGES * STAGE_BYTES;
 // ring, mbarriers, per-warp (m, l) [4][16] x 2, per-warp O [4][G][128], flag word
 template <int G>
@@ -71,13 +75,18 @@ struct BalArgs {
 __device__ __forceinline__ long long run_start(int k, long long P, int NG) { return (long long)k * P / NG; }
 // The group whose run holds page x.
 __device__ __forceinline__ int run_of(long long x, long long P, int NG) { return (int)(((x + 1) * NG - 1) / P); }
-// The sequence whose pages [indptr[b], indptr[b+1]) hold page x (x < indptr[B]).
-__device__ __forceinline__ int seq_of(const int* indptr, int B, long long x) {
-    int lo = 0, hi = B;
-    while (hi - lo > 1) {
-        const int mid = (lo + hi) >> 1;
-        if (__ldg(indptr + mid) <= x) lo = mid;
-        else hi = mid;
+// The sequence whose pages [indptr[b], indptr[b+1]) hold page x (x < indptr[B]): the last b
+// with indptr[b] <= x. The whole warp searches 32 ways per round (one dependent load per
+// round instead of log2(B)); every lane returns the same b.
+__device__ __forceinline__ int seq_of(const int* indptr, int B, long long x, int lane) {
+    int lo = 0, n = B;                                    // b lies in [lo, lo + n); indptr[lo] <= x
+    while (n > 1) {
+        const int step = (n + 31) >> 5;
+        const int off = lane * step;
+        const bool le = off < n && __ldg(indptr + lo + off) <= x;
+        const int j = 31 - __clz(__ballot_sync(0xffffffffu, le));   // lane 0 always holds
+        lo += j * step;
+        n = min(step, n - j * step);
     }
     return lo;
 }
@@ -134,7 +143,7 @@ decode_balanced_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_con
     const uint64_t deadline = globaltimer() + a.timeout_ns;
 
     // the sequence and page of the run's first page
-    const int b0 = seq_of(a.indptr, a.B, x0);
+    const int b0 = seq_of(a.indptr, a.B, x0, lane);
     const int pg0 = (int)(x0 - __ldg(a.indptr + b0));
 
     if (warp == BCONS) {
@@ -274,37 +283,68 @@ decode_balanced_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_con
     __threadfence();                                      // this thread's partial stores
     pdl_wait();                                           // the counts were cleared
     consumer_sync();
+    if (threadIdx.x < nsplit) {                           // both units counted in one round trip
+        const int si = threadIdx.x;
+        const unsigned arrived = atomicAdd(a.count + split_b[si] * a.Hkv + h, 1u);
+        s_last[si] = arrived == (unsigned)(split_last[si] - split_first[si]);
+        __threadfence();
+    }
+    consumer_sync();
+    // Slot columns a thread keeps in registers per round trip of the merge.
+    constexpr int CT = G >= 16 ? 2 : G >= 8 ? 4 : 8;
     for (int si = 0; si < nsplit; si++) {
+        if (!s_last[si]) continue;                        // uniform: s_last is shared
         const int sb = split_b[si], cf = split_first[si], cl = split_last[si];
-        const int u = sb * a.Hkv + h;
-        if (threadIdx.x == 0) {
-            const bool last = atomicAdd(a.count + u, 1u) == (unsigned)(cl - cf);
-            s_last[0] = last;
-            __threadfence();
-        }
+        // Slots cf..cl of the unit are contiguous. Their lse rows are staged in o_red (free
+        // after the last unit; nc <= NG <= BMAX_GROUPS) while the first CT slots' columns are
+        // already in flight. Thread d owns column d of every head row.
+        const int nc = cl - cf + 1;
+        const size_t first = (size_t)h * (a.B + NG) + sb + cf;
+        const int d = threadIdx.x;
+        const float* po = a.part_o + first * G * D + d;
+        float v[CT][G];
+        auto load_cols = [&](int c0) {
+#pragma unroll
+            for (int j = 0; j < CT; j++)
+#pragma unroll
+                for (int gq = 0; gq < G; gq++)
+                    v[j][gq] = c0 + j < nc ? __ldcg(po + ((size_t)(c0 + j) * G + gq) * D) : 0.f;
+        };
+        load_cols(0);
+        float* s_lse = o_red;                             // [nc][G]
+        for (int i = threadIdx.x; i < nc * G; i += BCONS * 32) s_lse[i] = __ldcg(a.part_lse + first * G + i);
         consumer_sync();
-        if (s_last[0]) {
-            const size_t slot_base = (size_t)h * (a.B + NG) + sb;
-            for (int idx = threadIdx.x; idx < G * D; idx += BCONS * 32) {
-                const int gq = idx / D, d = idx - gq * D;
-                float M = -INFINITY;
-                for (int cc = cf; cc <= cl; cc++)
-                    M = fmaxf(M, __ldcg(a.part_lse + (slot_base + cc) * G + gq));
-                float L = 0.f, O = 0.f;
-                if (M != -INFINITY)
-                    for (int cc = cf; cc <= cl; cc++) {
-                        const float li = __ldcg(a.part_lse + (slot_base + cc) * G + gq);
-                        if (li == -INFINITY) continue;
-                        const float w = ex2((li - M) * LOG2E);
-                        L += w;
-                        O += w * __ldcg(a.part_o + ((slot_base + cc) * G + gq) * D + d);
-                    }
-                const size_t row = (size_t)sb * a.Hq + (size_t)h * G + gq;
-                a.out[row * D + d] = __float2half_rn(L > 0.f ? O / L : 0.f);
-                if (d == 0) a.lse[row] = L > 0.f ? M + logf(L) : -INFINITY;
+        float M[G], L[G], O[G];
+#pragma unroll
+        for (int gq = 0; gq < G; gq++) {
+            float m = -INFINITY;
+            for (int c = 0; c < nc; c++) m = fmaxf(m, s_lse[c * G + gq]);
+            M[gq] = m;
+            L[gq] = 0.f;
+            O[gq] = 0.f;
+        }
+        for (int c0 = 0; c0 < nc; c0 += CT) {
+            if (c0) load_cols(c0);
+#pragma unroll
+            for (int j = 0; j < CT; j++) {
+                if (c0 + j >= nc) break;
+#pragma unroll
+                for (int gq = 0; gq < G; gq++) {
+                    const float li = s_lse[(c0 + j) * G + gq];
+                    if (M[gq] == -INFINITY || li == -INFINITY) continue;
+                    const float w = ex2((li - M[gq]) * LOG2E);
+                    L[gq] += w;
+                    O[gq] += w * v[j][gq];
+                }
             }
         }
-        consumer_sync();                                  // s_last reused
+#pragma unroll
+        for (int gq = 0; gq < G; gq++) {
+            const size_t row = (size_t)sb * a.Hq + (size_t)h * G + gq;
+            a.out[row * D + d] = __float2half_rn(L[gq] > 0.f ? O[gq] / L[gq] : 0.f);
+            if (d == 0) a.lse[row] = L[gq] > 0.f ? M[gq] + logf(L[gq]) : -INFINITY;
+        }
+        consumer_sync();                                  // o_red reused by the next unit
     }
 }
 
@@ -392,7 +432,7 @@ ckl_status check_balanced(const ckl_decode_params* p, int* G) {
 
 // Launch width: one wave of resident CTAs, rounded down to whole groups of Hkv CTAs.
 int balanced_grid(const DeviceInfo* di, const BalSetup* bs, int G, int Hkv) {
-    return std::max(1, di->sms * bs->per_sm[G] / Hkv) * Hkv;
+    return std::min(std::max(1, di->sms * bs->per_sm[G] / Hkv), BMAX_GROUPS) * Hkv;
 }
 
 size_t balanced_slots(const ckl_decode_params* p, int grid) {
