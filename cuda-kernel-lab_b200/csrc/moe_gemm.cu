@@ -7,9 +7,9 @@
 // The reference runs it on CUDA cores (fp32 FMA per weight per row); on B200 that is
 // compute-bound from ~4 rows per expert. Here the dequantised weights are the A operand of
 // mma.sync.m16n8k16 (16 output columns x 16 k, "swap-AB") and up to 8 tokens per MMA are
-// the B operand: a warp decodes 8 int4 weights with ~13 integer/half instructions (fp16
-// magic number, exact (q - z), times the fp16 group scale) and issues one MMA per 8 tokens,
-// accumulating in fp32.
+// the B operand: a warp decodes 8 int4 weights with 9 instructions (fp16 magic number,
+// exact (q - z); the fp16 group scale is applied to an fp32 group accumulator) and issues
+// one MMA per 8 tokens, accumulating in fp32.
 //
 // A CTA owns one 64-column quad of one expert: warp 4 is a producer that, per 128-wide k
 // group, issues one cp.async.bulk of the quad's 4 contiguous records (codes + embedded
@@ -40,28 +40,42 @@ constexpr int XSTRIDE = GPS * 256 + 64;      // smem bytes per staged token row 
                                              // rows a quarter-warp reads land on disjoint banks)
 constexpr int MAX_STAGES = 16;
 constexpr int TMAX = 2;                      // token tiles (8 rows each) per pass
-constexpr uint32_t MAGIC = 0x64006400u;      // fp16 1024.0 in both halves
-
-__device__ __forceinline__ __half2 as_h2(uint32_t x) { return *reinterpret_cast<__half2*>(&x); }
-__device__ __forceinline__ uint32_t as_u32(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
 
 // int4 fragment decode to (q - z) in fp16, exact: z of column g (zc0 = half2(1024+z)) and
-// of column g+8 (zc1n = -half2(64+z)); nibble order in moe_common.cuh. 9 instructions.
+// of column g+8 (zc1n = -half2(64+z)); nibble order in moe_common.cuh. 9 instructions on
+// 32-bit registers: (w & 0x000F000F) | 0x6400_6400 is half2(1024 + q) for nibbles 0 and 4,
+// (w & 0x00F000F0) | 0x6400_6400 is half2(1024 + 16 q) for nibbles 1 and 5 (scaled back by
+// 1/16 = 0x2C00 in the fma), and the same on w >> 8 for nibbles 2, 6 and 3, 7.
 __device__ __forceinline__ void dec4(uint32_t w, uint32_t zc0, uint32_t zc1n, uint32_t (&a)[4]) {
-    const __half2 sixteenth = __float2half2_rn(0.0625f);
-    const uint32_t w8 = w >> 8;
-    a[0] = as_u32(__hsub2(as_h2((w & 0x000F000Fu) | MAGIC), as_h2(zc0)));
-    a[1] = as_u32(__hfma2(as_h2((w & 0x00F000F0u) | MAGIC), sixteenth, as_h2(zc1n)));
-    a[2] = as_u32(__hsub2(as_h2((w8 & 0x000F000Fu) | MAGIC), as_h2(zc0)));
-    a[3] = as_u32(__hfma2(as_h2((w8 & 0x00F000F0u) | MAGIC), sixteenth, as_h2(zc1n)));
+    asm("{\n\t.reg .b32 t0, t1, t2, t3, w8;\n\t"
+        "shr.b32 w8, %4, 8;\n\t"
+        "lop3.b32 t0, %4, 0x000F000F, 0x64006400, 0xEA;\n\t"
+        "lop3.b32 t1, %4, 0x00F000F0, 0x64006400, 0xEA;\n\t"
+        "lop3.b32 t2, w8, 0x000F000F, 0x64006400, 0xEA;\n\t"
+        "lop3.b32 t3, w8, 0x00F000F0, 0x64006400, 0xEA;\n\t"
+        "sub.rn.f16x2 %0, t0, %5;\n\t"
+        "fma.rn.f16x2 %1, t1, %7, %6;\n\t"
+        "sub.rn.f16x2 %2, t2, %5;\n\t"
+        "fma.rn.f16x2 %3, t3, %7, %6;\n\t}"
+        : "=r"(a[0]), "=r"(a[1]), "=r"(a[2]), "=r"(a[3])
+        : "r"(w), "r"(zc0), "r"(zc1n), "r"(0x2C002C00u));
 }
-// int8 fragment decode: offset-binary q + 128 -> q exactly.
+// int8 fragment decode: offset-binary q + 128 -> q exactly ((w & 0x00FF00FF) | 0x6400_6400
+// is half2(1024 + q + 128); subtract half2(1152) = 0x6480).
 __device__ __forceinline__ void dec8(uint32_t w0, uint32_t w1, uint32_t (&a)[4]) {
-    const __half2 bias = as_h2(0x64806480u);   // 1024 + 128
-    a[0] = as_u32(__hsub2(as_h2((w0 & 0x00FF00FFu) | MAGIC), bias));
-    a[1] = as_u32(__hsub2(as_h2(((w0 >> 8) & 0x00FF00FFu) | MAGIC), bias));
-    a[2] = as_u32(__hsub2(as_h2((w1 & 0x00FF00FFu) | MAGIC), bias));
-    a[3] = as_u32(__hsub2(as_h2(((w1 >> 8) & 0x00FF00FFu) | MAGIC), bias));
+    asm("{\n\t.reg .b32 t0, t1, t2, t3, u0, u1;\n\t"
+        "shr.b32 u0, %4, 8;\n\t"
+        "shr.b32 u1, %5, 8;\n\t"
+        "lop3.b32 t0, %4, 0x00FF00FF, 0x64006400, 0xEA;\n\t"
+        "lop3.b32 t1, u0, 0x00FF00FF, 0x64006400, 0xEA;\n\t"
+        "lop3.b32 t2, %5, 0x00FF00FF, 0x64006400, 0xEA;\n\t"
+        "lop3.b32 t3, u1, 0x00FF00FF, 0x64006400, 0xEA;\n\t"
+        "sub.rn.f16x2 %0, t0, %6;\n\t"
+        "sub.rn.f16x2 %1, t1, %6;\n\t"
+        "sub.rn.f16x2 %2, t2, %6;\n\t"
+        "sub.rn.f16x2 %3, t3, %6;\n\t}"
+        : "=r"(a[0]), "=r"(a[1]), "=r"(a[2]), "=r"(a[3])
+        : "r"(w0), "r"(w1), "r"(0x64806480u));
 }
 
 struct GemmArgs {
