@@ -63,29 +63,45 @@ route_kernel(const float* __restrict__ logits, int T, int E, int k, int* __restr
             s_lg[(i / E) * lg_stride + i % E] = __ldg(logits + i);
     __syncthreads();
 
-    // top-k by rank counting, one warp per token: lane l ranks experts l, l+32, ... against
-    // all E logits of the token, rank(e) = #{e' : v_e' > v_e or (v_e' = v_e and e' < e)}
-    // (the reference's order: larger value first, ties to the lower id, common/moe.cuh:
-    // 55-59). Expert e is chosen iff rank(e) < k, and rank(e) is its slot. The compares are
-    // independent, so the loop pipelines instead of chaining k argmax rounds.
+    // top-k, one warp per token: lane l holds experts l, l+32, ... as order-preserving keys of
+    // their logits (-0 folded into +0, so equal logits tie); k rounds of a warp argmax (max key
+    // by one reduction, then the lowest id holding it by another), the winner's key retired.
+    // This is the reference's order: larger value first, ties to the lower id
+    // (common/moe.cuh:55-59), and round r fills slot r.
     const int nwarps = blockDim.x >> 5;
+    const int nj = (E + 31) >> 5;                          // experts per lane (<= MAX_E / 32)
     for (int t = warp; t < T; t += nwarps) {
         const float* lg = staged ? s_lg + (size_t)t * lg_stride : logits + (size_t)t * E;
-        for (int e = lane; e < E; e += 32) {
-            const float v = lg[e];
-            int rank = 0;
-            int e2 = 0;
-            for (; e2 + 4 <= E; e2 += 4) {
-                const float a0 = lg[e2], a1 = lg[e2 + 1], a2 = lg[e2 + 2], a3 = lg[e2 + 3];
-                rank += (a0 > v || (a0 == v && e2 < e)) + (a1 > v || (a1 == v && e2 + 1 < e)) +
-                        (a2 > v || (a2 == v && e2 + 2 < e)) + (a3 > v || (a3 == v && e2 + 3 < e));
+        uint32_t key[MAX_E / 32];
+#pragma unroll
+        for (int j = 0; j < MAX_E / 32; j++) {
+            const int e = lane + 32 * j;
+            uint32_t u = 0;                                // below every logit's key
+            if (j < nj && e < E) {
+                uint32_t bits = __float_as_uint(lg[e]);
+                if (bits == 0x80000000u) bits = 0u;
+                u = (bits & 0x80000000u) ? ~bits : (bits | 0x80000000u);
             }
-            for (; e2 < E; e2++) rank += lg[e2] > v || (lg[e2] == v && e2 < e);
-            if (rank < k) {
-                s_ids[t * k + rank] = e;
-                s_selv[t * MAX_K + rank] = v;
-                ids[t * k + rank] = e;
-                atomicAdd(&s_cnt[e], 1);                 // integer histogram: order-free
+            key[j] = u;
+        }
+        for (int r = 0; r < k; r++) {
+            uint32_t bk = key[0];
+            int bj = 0;
+#pragma unroll
+            for (int j = 1; j < MAX_E / 32; j++) {
+                if (j >= nj) break;
+                if (key[j] > bk) { bk = key[j]; bj = j; }   // ties keep the lower id
+            }
+            const uint32_t m = __reduce_max_sync(0xffffffffu, bk);
+            const int e = (int)__reduce_min_sync(0xffffffffu, bk == m ? (uint32_t)(lane + 32 * bj) : 0xffffffffu);
+#pragma unroll
+            for (int j = 0; j < MAX_E / 32; j++)
+                if (lane + 32 * j == e) key[j] = 0u;
+            if (lane == 0) {
+                s_ids[t * k + r] = e;
+                s_selv[t * MAX_K + r] = lg[e];
+                ids[t * k + r] = e;
+                atomicAdd(&s_cnt[e], 1);                   // integer histogram: order-free
             }
         }
         __syncwarp();

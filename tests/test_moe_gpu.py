@@ -147,6 +147,31 @@ def test_expert_gemm_reference_case(ckl, oracle, dev, bits, ks):
     assert np.all(np.abs(got - ref) <= 2e-3 + 1e-2 * np.abs(ref))
 
 
+@pytest.mark.parametrize("asym", [True, False])
+@pytest.mark.parametrize("ks", [1, 2, 4])
+def test_expert_gemm_int4_tile_multiple_width(ckl, oracle, dev, asym, ks):
+    """int4 at a width of whole 64-column quads: the reference case's generators at d=1024,
+    f=384, T=40, E=8, top-2 -- experts with more than 16 rows run in several passes, expert
+    3 is empty -- K split 1, 2 and 4 ways, asymmetric and symmetric codes."""
+    T, E, k, d, f = 40, 8, 2, 1024, 384
+    lg = oracle.make_logits(T, E, 5, 3)
+    X = oracle.init_uniform((T, d), 6, 1.0)
+    W = oracle.init_uniform((E, d, f), 7, 1.0 / np.sqrt(d))
+    r = ckl.route_and_permute(T_(lg, dev), T_(X, dev), k)
+    offs = r["offsets"].cpu().numpy()
+    assert offs[4] == offs[3] and np.diff(offs).max() > 16
+    q = ckl.QuantWeights(4, T_(W, dev), group=128, asym=asym)
+    import torch
+    Yp = torch.zeros((T * k, f), dtype=torch.float16, device=dev)
+    q.run(r["Xp"], Yp, r["offsets"], T * k, force_ksplit=ks)
+    torch.cuda.synchronize()
+    ckl.check_device_error()
+    ref = oracle.expert_gemm(r["Xp"].cpu().numpy(), q.dequant().cpu().numpy(), offs)
+    got = Yp.float().cpu().numpy()
+    assert rel_rms(got, ref) <= REL_RMS
+    assert np.all(np.abs(got - ref) <= 2e-3 + 1e-2 * np.abs(ref))
+
+
 def _layer_weights(ckl, oracle, dev, E, d, F, mode, seed=11):
     import torch
     Wg = oracle.normal((E, d, F), seed=seed, std=0.02)
