@@ -11,14 +11,16 @@
 // exact (q - z); the fp16 group scale is applied to an fp32 group accumulator) and issues
 // one MMA per 8 tokens, accumulating in fp32.
 //
-// A CTA owns one 64-column quad of one expert: warp 4 is a producer that, per 128-wide k
-// group, issues one cp.async.bulk of the quad's 4 contiguous records (codes + embedded
-// scales/zeros) per matrix (two for SwiGLU: gate and up) and one 256-byte copy of each token
-// row's k slice, into a multi-stage shared-memory ring with full/empty mbarriers (no
-// multicast). Warps 0-3 each compute one 16-column tile from the stage. The CTA's expert is
-// the j-th expert with rows, found on the device from the expert offsets, so the launch
-// needs no host sync: the grid is an upper bound (min(E, A) expert slots) and surplus CTAs
-// exit (02_moe_grouped_gemm.cu:95, 234-235).
+// A CTA owns one 64-column quad of one expert (over one K slice): warp 8 is a producer that,
+// per stage of two 128-wide k groups, issues one cp.async.bulk of the quad's 4 contiguous
+// records (codes + embedded scales/zeros) per group and matrix (two matrices for SwiGLU:
+// gate and up) and one copy of each token row's k slice, into a multi-stage shared-memory
+// ring with full/empty mbarriers (no multicast). Warps 0-7 consume: warp w computes the
+// 16-column tile w % 4 on group w / 4 of the stage, and the two warps of a tile add their
+// sums through shared memory at the end of a pass. The CTA's expert is the j-th expert with
+// rows, found on the device from the expert offsets, so the launch needs no host sync: the
+// grid is an upper bound (min(E, A) expert slots) and surplus CTAs exit
+// (02_moe_grouped_gemm.cu:95, 234-235).
 
 #include <algorithm>
 #include <mutex>
