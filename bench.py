@@ -207,6 +207,32 @@ def measured_peak():
         return 6650.0, "fallback"
 
 
+NOMINAL_HBM_GBS = 7700.0     # B200 HBM3e, HGX figure (8000 on DGX)
+
+
+def stream_read_ceiling(ckl, dev, gib=2, iters=10):
+    """The reference's own bandwidth denominator: its stream_read probe
+    (01_decode_attention.cu:257-265, ckl_stream_read) over a gib-GiB buffer, GB/s (CUDA
+    events on the launching stream, after 3 warm-up reads; the buffer is 16x L2)."""
+    import torch
+    buf = torch.zeros(gib << 30, dtype=torch.uint8, device=dev)
+    sink = torch.zeros(4, dtype=torch.int32, device=dev)
+    stream = torch.cuda.current_stream()
+    for _ in range(3):
+        ckl.stream_read(buf, sink, stream)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for _ in range(iters):
+        ckl.stream_read(buf, sink, stream)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    gbs = buf.numel() / (e0.elapsed_time(e1) / iters * 1e-3) / 1e9
+    del buf
+    torch.cuda.empty_cache()
+    return gbs
+
+
 def committed_traffic(kernel, workload):
     """DRAM bytes per launch from a committed ncu summary (profiles/traffic.json)."""
     try:
@@ -1116,6 +1142,7 @@ def run_ours(args):
 
     peak, peak_kind = measured_peak()
     achieved = byts / (kern_ms * 1e-3) / 1e9
+    srd = stream_read_ceiling(ckl, dev)
     extras = {}
     if not args.no_extras:
         del k, v
@@ -1155,6 +1182,12 @@ def run_ours(args):
             "data": "synthetic: U(-1,1) fp16 K/V/q filled on device, seeded shuffled page table",
             "config": config_of(args.workload, lens, world),
             "frac_of_hbm": byts * world / (ms_max * 1e-3) / 1e9 / (peak * world),
+            "denominators": {"measured_copy_gbs": peak, "reference_stream_read_gbs": srd,
+                             "nominal_hbm_gbs": NOMINAL_HBM_GBS,
+                             "frac_of_stream_read": byts / (ms_max * 1e-3) / 1e9 / srd,
+                             "frac_of_nominal": byts / (ms_max * 1e-3) / 1e9 / NOMINAL_HBM_GBS,
+                             "stream_read": "this GPU, 2 GiB, ckl_stream_read (the reference's "
+                                            "stream_read probe), mean of 10 reads after 3 warm-up"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_source": peak_kind,
                          "kernel": "decode_partial_kernel<4>",
