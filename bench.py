@@ -333,7 +333,7 @@ class ColdTimer:
         self.flush = torch.empty(512 << 20, dtype=torch.uint8, device=dev)
         self.world = world
 
-    def __call__(self, fn, iters=15, warmup=3):
+    def __call__(self, fn, iters=31, warmup=3):
         import torch
         for _ in range(warmup):
             fn()
@@ -388,7 +388,7 @@ def paged_batch(lens, dev, seed, Lp=0):
 
 def sweep_config2(ckl, dev, timer, peak):
     """Every config-2 shape through ckl_decode_attention (the reference's chunked split) and
-    ckl_decode_attention_balanced, cold L2, median of 15."""
+    ckl_decode_attention_balanced, cold L2, median of 31."""
     import torch
     rows = {}
     for name in ("1x32768", "8x8192", "64x1024", "256x4096", "ragged256"):
@@ -625,7 +625,7 @@ def bench_moe(ckl, dev, timer, peak, n_layers=8):
                                                                       (layers[0][0][2], False))
                                                       if w.workspace_size(T * k, sw) > 0)}
     res["method"] = (f"{n_layers} layers with distinct weights in one CUDA graph, L2 flushed "
-                     "before each replay, per-layer median of 15; PDL between the layer's kernels")
+                     "before each replay, per-layer median of 31; PDL between the layer's kernels")
     del layers
     torch.cuda.empty_cache()
     return res
@@ -727,7 +727,7 @@ def bench_grouped_gemm(ckl, dev, timer, peak):
                      "us_cublas_per_expert_loop": round(t_ref * 1e3, 1)}
         del W, Xp, Yp, r
         torch.cuda.empty_cache()
-    res["method"] = "cold L2 (512 MB memset before each sample), median of 15; bytes = active experts' fp16 weights + Xp + Yp"
+    res["method"] = "cold L2 (512 MB memset before each sample), median of 31; bytes = active experts' fp16 weights + Xp + Yp"
     return res
 
 
@@ -1168,7 +1168,7 @@ def run_ours(args):
             if run("config5_mixtral_layer_tp_ep"):
                 extras["config5_mixtral_layer_tp_ep"] = bench_mixtral_ep(ckl, dev, timer, peak,
                                                                          rank, world, ex)
-        extras["extras_timing"] = ("cold L2 (512 MB memset before each sample), median of 15"
+        extras["extras_timing"] = ("cold L2 (512 MB memset before each sample), median of 31"
                                    + ("; ranks start each sample together (barrier), max over "
                                       "ranks" if world > 1 else ""))
     cpu = None
