@@ -547,7 +547,8 @@ def bench_cascade_tree(ckl, dev, timer, peak):
 
 def _moe_active_bytes(q, ids_np):
     """Algorithmic bytes of one layer step: packed weights + scales + zeros of every active
-    expert (gate, up, down) + X in + out."""
+    expert (gate, up, down) + X in + out (the reference credits the active experts' weight
+    bytes, 03_moe_wq_decode.cu:527,551)."""
     import numpy as np
     active = len(np.unique(ids_np))
     return active * sum(w.bytes_per_expert() for w in q)

@@ -562,7 +562,8 @@ class QuantWeights:
         return self
 
     def bytes_per_expert(self):
-        """Algorithmic bytes of one expert: codes + scales (+ zero points)."""
+        """Algorithmic bytes of one expert: codes + scales (+ zero points), the bytes a
+        decode step must stream for it (03_moe_wq_decode.cu:527,551 credit the same)."""
         b = self.K * self.N * self.bits // 8
         if self.bits != 16:
             b += (self.K // self.group) * self.N * 2
