@@ -106,6 +106,32 @@ def test_routing_bit_exact(ckl, oracle, dev, T, E, k, disable, seed):
     assert np.array_equal(Xp[inv], X[flat])
 
 
+@pytest.mark.parametrize("T,E,k", [(64, 64, 6), (33, 8, 2), (16, 256, 8)])
+def test_routing_ties_go_to_the_lower_id(ckl, oracle, dev, T, E, k):
+    """Logits drawn from 5 integer values (many exact ties), a quarter of the zeros negative:
+    slot order is larger logit first, equal logits (-0 equal to +0) to the lower expert id,
+    as in the reference (common/moe.cuh:55-59); ids bit-exact against the host restatement
+    and, where it was compiled, the reference's own router_topk."""
+    rng = np.random.default_rng(T * 1000 + E)
+    lg = rng.integers(-2, 3, size=(T, E)).astype(np.float32)
+    neg0 = (lg == 0) & (rng.random((T, E)) < 0.25)
+    lg[neg0] = -0.0
+    assert np.any(np.signbit(lg) & (lg == 0))
+    r = ckl.route_and_permute(T_(lg, dev), None, k, permute=False)
+    ids, wts = oracle.route(lg, k)
+    assert np.array_equal(r["ids"].cpu().numpy(), ids)
+    assert np.allclose(r["wts"].cpu().numpy(), wts, rtol=2e-6, atol=0)
+    if os.path.exists(REF03):
+        import ctypes as C
+        import torch
+        rid = torch.empty((T, k), dtype=torch.int32, device=dev)
+        rw = torch.empty((T, k), dtype=torch.float32, device=dev)
+        d_lg = T_(lg, dev)
+        assert oracle.ref03().ref03_router_topk_device(C.c_void_p(d_lg.data_ptr()), C.c_void_p(rid.data_ptr()),
+                                                       C.c_void_p(rw.data_ptr()), T, E, k) == 0
+        assert torch.equal(r["ids"], rid)
+
+
 @pytest.mark.skipif(not os.path.exists(REF03), reason="reference not compiled here")
 def test_routing_matches_reference_router_kernel(ckl, oracle, dev):
     """Same ids as the reference's own router_topk kernel (common/moe.cuh:23-72)."""
