@@ -576,7 +576,7 @@ class GraphStep:
         self.g.replay()
 
 
-def bench_moe(ckl, dev, timer, peak, n_layers=8, layout=0):
+def bench_moe(ckl, dev, timer, peak, n_layers=8):
     """W4A16 (asym int4 g128) SwiGLU MoE layer, E=64, top-6, d=2048,
     F=1408, T in {1,4,16,64}; weights N(0,0.02), X and logits N(0,1).
 
@@ -591,8 +591,8 @@ def bench_moe(ckl, dev, timer, peak, n_layers=8, layout=0):
     mk = lambda *sh: (torch.randn(*sh, generator=g, device=dev) * 0.02).half()
     layers = []
     for _ in range(n_layers):
-        q = [ckl.QuantWeights(4, mk(E, d, F), group=128, asym=True, layout=layout) for _ in range(2)]
-        q.append(ckl.QuantWeights(4, mk(E, F, d), group=128, asym=True, layout=layout))
+        q = [ckl.QuantWeights(4, mk(E, d, F), group=128, asym=True) for _ in range(2)]
+        q.append(ckl.QuantWeights(4, mk(E, F, d), group=128, asym=True))
         layers.append((q, ckl.MoeLayer(*q)))
     res = {}
     for T in (1, 4, 16, 64):

@@ -60,7 +60,7 @@ class CascadeTreePlan(C.Structure):
 class MoeWeights(C.Structure):
     """ckl_moe_weights (the packed buffers of QuantWeights, 03_moe_wq_decode.cu:281-333)."""
     _fields_ = [("bits", C.c_int), ("E", C.c_int), ("K", C.c_int), ("N", C.c_int),
-                ("group", C.c_int), ("asym", C.c_int), ("layout", C.c_int), ("packed", C.c_void_p),
+                ("group", C.c_int), ("asym", C.c_int), ("packed", C.c_void_p),
                 ("scales", C.c_void_p), ("zeros", C.c_void_p)]
 
 
@@ -125,7 +125,6 @@ _SIGS = {
     "ckl_cascade_decode": (C.c_int, [C.POINTER(CascadePlan), C.c_void_p, C.c_void_p,
                                      C.c_void_p, C.c_size_t, C.c_void_p]),
     "ckl_moe_packed_bytes": (C.c_size_t, [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int]),
-    "ckl_moe_packed_bytes_layout": (C.c_size_t, [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int]),
     "ckl_moe_scale_count": (C.c_size_t, [C.c_int, C.c_int, C.c_int, C.c_int]),
     "ckl_moe_zero_words": (C.c_size_t, [C.c_int, C.c_int, C.c_int, C.c_int]),
     "ckl_moe_pack_weights": (C.c_int, [C.c_void_p, C.POINTER(MoeWeights), C.c_void_p]),
@@ -499,16 +498,12 @@ def cascade_tree_decode(tp: CascadeTreePlan, out=None, lse=None, workspace=None,
 
 
 # ------------------------------------------------------------------ MoE
-LAYOUT_FRAGMENT, LAYOUT_COLUMN = 0, 1    # CKL_MOE_LAYOUT_*
-
-
 class QuantWeights:
     """QuantWeights (03_moe_wq_decode.cu:281-333): packs fp16 W [E][K][N] (a CUDA tensor)
     into the library's format. bits 4 (group 128; asym=True adds zero points), 8 (group 128
-    or group=K per output channel) or 16. layout=LAYOUT_COLUMN (int4, N % 128 == 0) packs
-    for the tcgen05 GEMM."""
+    or group=K per output channel) or 16."""
 
-    def __init__(self, bits, W, group=128, asym=False, layout=LAYOUT_FRAGMENT, stream=None):
+    def __init__(self, bits, W, group=128, asym=False, stream=None):
         torch = _torch()
         _need(W, torch.float16, "W")
         E, K, N = W.shape
@@ -516,17 +511,14 @@ class QuantWeights:
         if bits == 16:
             group = K
         self.bits, self.E, self.K, self.N, self.group, self.asym = bits, E, K, N, group, asym
-        self.layout = layout
         L = lib()
-        nbytes = L.ckl_moe_packed_bytes_layout(bits, E, K, N, group, layout)
-        if nbytes == 0:
-            raise CklError(f"QuantWeights: layout {layout} does not take bits={bits} group={group} N={N}")
-        self.packed = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+        self.packed = torch.empty(L.ckl_moe_packed_bytes(bits, E, K, N, group), dtype=torch.uint8,
+                                  device=dev)
         ns = L.ckl_moe_scale_count(E, K, N, group) if bits != 16 else 1
         self.scales = torch.empty(max(ns, 1), dtype=torch.float16, device=dev)
         nz = L.ckl_moe_zero_words(E, K, N, group) if asym else 1
         self.zeros = torch.zeros(max(nz, 1), dtype=torch.int32, device=dev)
-        self.w = MoeWeights(bits, E, K, N, group, int(asym), layout, self.packed.data_ptr(),
+        self.w = MoeWeights(bits, E, K, N, group, int(asym), self.packed.data_ptr(),
                             self.scales.data_ptr() if bits != 16 else None,
                             self.zeros.data_ptr() if asym else None)
         check(L.ckl_moe_pack_weights(_ptr(W), C.byref(self.w), _stream(stream)),
@@ -553,16 +545,15 @@ class QuantWeights:
               "ckl_moe_weights_file_info")
         self = cls.__new__(cls)
         self.bits, self.E, self.K, self.N = info.bits, info.E, info.K, info.N
-        self.group, self.asym, self.layout = info.group, bool(info.asym), info.layout
+        self.group, self.asym = info.group, bool(info.asym)
         L = lib()
-        self.packed = torch.empty(L.ckl_moe_packed_bytes_layout(info.bits, info.E, info.K, info.N,
-                                                                info.group, info.layout),
+        self.packed = torch.empty(L.ckl_moe_packed_bytes(info.bits, info.E, info.K, info.N, info.group),
                                   dtype=torch.uint8, device=device)
         ns = L.ckl_moe_scale_count(info.E, info.K, info.N, info.group) if info.bits != 16 else 1
         self.scales = torch.empty(max(ns, 1), dtype=torch.float16, device=device)
         nz = L.ckl_moe_zero_words(info.E, info.K, info.N, info.group) if info.asym else 1
         self.zeros = torch.zeros(max(nz, 1), dtype=torch.int32, device=device)
-        self.w = MoeWeights(info.bits, info.E, info.K, info.N, info.group, info.asym, info.layout,
+        self.w = MoeWeights(info.bits, info.E, info.K, info.N, info.group, info.asym,
                             self.packed.data_ptr(),
                             self.scales.data_ptr() if info.bits != 16 else None,
                             self.zeros.data_ptr() if info.asym else None)

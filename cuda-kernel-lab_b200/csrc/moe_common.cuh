@@ -92,38 +92,5 @@ __host__ __device__ inline void frag_coord(int ks, int lane, int j, int* k, int*
     *col = g + ((reg & 1) ? 8 : 0);
 }
 
-// ------------------------------------------------------------------ column layout (int4)
-// CKL_MOE_LAYOUT_COLUMN: int4, group 128, N a multiple of 128; the layout of the tensor-core
-// GEMM, whose decode threads each own one output column and write its k values into tensor
-// memory. Blocks of (expert e, 128-column tile mt, group grp), in the order [e][mt][grp]:
-//   codes   8192 B: [half h (k 64h..)][lane quarter q][plane p (k 32p..)][lane l][16 B] --
-//           the 16 B of (h, q, p, l) are 4 words of column 32q + l, word i holding
-//           k = 64h + 32p + 8i + {0, 2, 4, 6, 1, 3, 5, 7} in nibbles 0..7, so
-//           ((w >> 4j) & 0x000F000F) | 0x64006400 is half2(1024 + q) of k 2j, 2j+1 (+8i)
-//   scales   256 B: fp16 of columns 0..127
-//   zeros     64 B: 4-bit zero points, column c in nibble c % 8 of word c / 8 (8 for
-//           symmetric codes)
-constexpr int COL_TILE = 128;
-constexpr int COL_CODES = COL_TILE * KGROUP_STAGE / 2;          // 8192
-constexpr int COL_BLOCK = COL_CODES + COL_TILE * 2 + COL_TILE / 2;   // 8512
-static_assert(COL_BLOCK % 16 == 0, "column blocks are bulk-copied");
-
-__host__ __device__ inline size_t col_block_offset(int K, int N, int e, int mt, int grp) {
-    return (((size_t)e * (N / COL_TILE) + mt) * (K / KGROUP_STAGE) + grp) * COL_BLOCK;
-}
-__host__ __device__ inline size_t col_packed_bytes(int E, int K, int N) {
-    return (size_t)E * (N / COL_TILE) * (K / KGROUP_STAGE) * COL_BLOCK;
-}
-// Byte of the 16-byte chunk (h, q, p, lane) inside a block's codes.
-__host__ __device__ inline int col_chunk_offset(int h, int q, int p, int lane) {
-    return ((h * 4 + q) * 2 + p) * 512 + lane * 16;
-}
-// (word i, nibble j) of the chunk holding k offset r (0..31 within the plane).
-__host__ __device__ inline void col_nibble_of(int r, int* i, int* j) {
-    *i = r >> 3;
-    const int kk = r & 7;
-    *j = (kk >> 1) + 4 * (kk & 1);
-}
-
 }  // namespace moe
 }  // namespace ckl

@@ -445,18 +445,6 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ P, void* Y, int y
     }
 }
 
-// Launches the fixed-order sum of ks split-K partials in workspace into Y.
-ckl_status splitk_reduce(void* workspace, void* Y, int y_f32, int A, int N, int ks, bool swiglu,
-                         const int* row_dst, const int* a_rows, int dep, cudaStream_t s) {
-    const float* P = static_cast<const float*>(workspace);
-    int ksv = ks, Av = A, Nv = N;
-    void* rargs[] = {&P, &Y, &y_f32, &Av, &Nv, &ksv, &row_dst, &a_rows};
-    const void* rfn = swiglu ? reinterpret_cast<const void*>(splitk_reduce_kernel<true>)
-                             : reinterpret_cast<const void*>(splitk_reduce_kernel<false>);
-    CKL_CUDA_TRY(launch(rfn, dim3(256), dim3(256), 0, s, rargs, dep != 0));
-    return CKL_OK;
-}
-
 // ------------------------------------------------------------------ packing
 // Scales (and zeros) per (e, group, column) -- the quantisers of the oracle:
 //   symmetric (03_moe_wq_decode.cu:65-72): s = fp16(max|w| / qmax) (1 if 0)
@@ -584,65 +572,6 @@ __global__ void pack_kernel(const __half* W, const __half* S, const uint32_t* Z,
 
 // Dequantised fp32 weights [E][K][N] from the packed codes (for bit-exact checks): the
 // exact (q - z) * s of host_weight (03_moe_wq_decode.cu:336-348).
-// Column layout (moe_common.cuh, int4 group 128): one thread per 16-byte chunk (expert,
-// 128-column tile, group, half, lane quarter, plane, lane) writes its column's 32 codes; the
-// chunks of half 0 / plane 0 also write the block's scales and zero-point words.
-__global__ void pack_col_kernel(const __half* W, const __half* S, const uint32_t* Z, uint8_t* P,
-                                int E, int K, int N, int asym) {
-    const int mtiles = N / COL_TILE, ngr = K / KGROUP_STAGE;
-    const size_t total = (size_t)E * mtiles * ngr * 512;
-    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total;
-         i += (size_t)gridDim.x * blockDim.x) {
-        const int chunk = (int)(i & 511);
-        const size_t blk = i >> 9;
-        const int grp = (int)(blk % ngr);
-        const int mt = (int)((blk / ngr) % mtiles);
-        const int e = (int)(blk / ((size_t)ngr * mtiles));
-        const int lane = chunk & 31, p = (chunk >> 5) & 1, q = (chunk >> 6) & 3, h = chunk >> 8;
-        const int c = 32 * q + lane, col = mt * COL_TILE + c;
-        uint8_t* bp = P + col_block_offset(K, N, e, mt, grp);
-        uint32_t wv[4];
-        for (int wi = 0; wi < 4; wi++) {
-            uint32_t w = 0;
-            for (int j = 0; j < 8; j++) {
-                const int k = grp * KGROUP_STAGE + 64 * h + 32 * p + 8 * wi + (j & 3) * 2 + (j >> 2);
-                w |= (uint32_t)quant_code(W, S, Z, e, k, col, K, N, KGROUP_STAGE, 4, asym) << (4 * j);
-            }
-            wv[wi] = w;
-        }
-        *reinterpret_cast<uint4*>(bp + col_chunk_offset(h, q, p, lane)) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
-        if (h == 0 && p == 0) {
-            const size_t prow = (size_t)e * ngr + grp;
-            reinterpret_cast<__half*>(bp + COL_CODES)[c] = S[prow * N + col];
-            if ((c & 7) == 0)
-                reinterpret_cast<uint32_t*>(bp + COL_CODES + 2 * COL_TILE)[c >> 3] =
-                    asym ? Z[prow * (N / 8) + col / 8] : 0x88888888u;
-        }
-    }
-}
-
-// The column layout's dequantised weights, from the block's own codes, scales and zeros.
-__global__ void dequant_col_kernel(const uint8_t* P, float* Wd, int E, int K, int N) {
-    const size_t total = (size_t)E * K * N;
-    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total;
-         i += (size_t)gridDim.x * blockDim.x) {
-        const int n = (int)(i % N);
-        const int k = (int)((i / N) % K);
-        const int e = (int)(i / ((size_t)N * K));
-        const int mt = n / COL_TILE, c = n % COL_TILE, q = c >> 5, lane = c & 31;
-        const int grp = k / KGROUP_STAGE, kk = k % KGROUP_STAGE, h = kk >> 6, p = (kk >> 5) & 1;
-        int wi, j;
-        col_nibble_of(kk & 31, &wi, &j);
-        const uint8_t* bp = P + col_block_offset(K, N, e, mt, grp);
-        const uint32_t w = reinterpret_cast<const uint32_t*>(bp + col_chunk_offset(h, q, p, lane))[wi];
-        const int code = (int)((w >> (4 * j)) & 15u);
-        const int z = (int)((reinterpret_cast<const uint32_t*>(bp + COL_CODES + 2 * COL_TILE)[c >> 3] >>
-                             (4 * (c & 7))) & 15u);
-        const float sc = __half2float(reinterpret_cast<const __half*>(bp + COL_CODES)[c]);
-        Wd[i] = (float)(code - z) * sc;
-    }
-}
-
 __global__ void dequant_kernel(const uint8_t* P, const __half* S, const uint32_t* Z, float* Wd,
                                int E, int K, int N, int group, int bits, int asym) {
     const size_t total = (size_t)E * K * N;
@@ -734,11 +663,6 @@ ckl_status check_weights(const ckl_moe_weights* w, const char* what) {
     if (!w->packed || (w->bits != 16 && !w->scales) || (w->asym && !w->zeros))
         return fail(CKL_INVALID_ARG, "%s: NULL weight buffer", what);
     if ((uintptr_t)w->packed & 15) return fail(CKL_INVALID_ARG, "%s: packed must be 16-byte aligned", what);
-    if (w->layout != CKL_MOE_LAYOUT_FRAGMENT && w->layout != CKL_MOE_LAYOUT_COLUMN)
-        return fail(CKL_INVALID_ARG, "%s: layout=%d", what, w->layout);
-    if (w->layout == CKL_MOE_LAYOUT_COLUMN && (w->bits != 4 || w->N % COL_TILE))
-        return fail(CKL_UNSUPPORTED_SHAPE, "%s: the column layout takes int4 with N %% 128 == 0 (bits=%d N=%d)",
-                    what, w->bits, w->N);
     return CKL_OK;
 }
 
@@ -767,14 +691,6 @@ size_t ckl_moe_packed_bytes(int bits, int E, int K, int N, int group) {
     return packed_bytes(bits, bits == 16 ? K : group, E, K, N);
 }
 
-size_t ckl_moe_packed_bytes_layout(int bits, int E, int K, int N, int group, int layout) {
-    if (layout == CKL_MOE_LAYOUT_FRAGMENT) return ckl_moe_packed_bytes(bits, E, K, N, group);
-    if (layout != CKL_MOE_LAYOUT_COLUMN || bits != 4 || group != KGROUP_STAGE || E <= 0 || K <= 0 ||
-        K % KGROUP_STAGE || N <= 0 || N % COL_TILE)
-        return 0;
-    return col_packed_bytes(E, K, N);
-}
-
 size_t ckl_moe_scale_count(int E, int K, int N, int group) {
     return group > 0 ? (size_t)E * (K / group) * N : 0;
 }
@@ -796,17 +712,11 @@ ckl_status ckl_moe_pack_weights(const void* W, ckl_moe_weights* w, void* stream)
                                                  group, w->bits, w->asym);
         CKL_CUDA_TRY(cudaGetLastError());
     }
-    if (w->layout == CKL_MOE_LAYOUT_COLUMN)
-        pack_col_kernel<<<2048, 256, 0, s>>>(static_cast<const __half*>(W),
-                                             static_cast<const __half*>(w->scales),
-                                             static_cast<const uint32_t*>(w->zeros),
-                                             static_cast<uint8_t*>(w->packed), w->E, w->K, w->N, w->asym);
-    else
-        pack_kernel<<<2048, 256, 0, s>>>(static_cast<const __half*>(W),
-                                         static_cast<const __half*>(w->scales),
-                                         static_cast<const uint32_t*>(w->zeros),
-                                         static_cast<uint8_t*>(w->packed), w->E, w->K, w->N, group,
-                                         w->bits, w->asym);
+    pack_kernel<<<2048, 256, 0, s>>>(static_cast<const __half*>(W),
+                                     static_cast<const __half*>(w->scales),
+                                     static_cast<const uint32_t*>(w->zeros),
+                                     static_cast<uint8_t*>(w->packed), w->E, w->K, w->N, group,
+                                     w->bits, w->asym);
     CKL_CUDA_TRY(cudaGetLastError());
     return CKL_OK;
 }
@@ -815,14 +725,10 @@ ckl_status ckl_moe_dequant_weights(const ckl_moe_weights* w, float* W_out, void*
     ckl_status st = check_weights(w, "moe_dequant_weights");
     if (st != CKL_OK) return st;
     if (!W_out) return fail(CKL_INVALID_ARG, "moe_dequant_weights: output NULL");
-    if (w->layout == CKL_MOE_LAYOUT_COLUMN)
-        dequant_col_kernel<<<2048, 256, 0, (cudaStream_t)stream>>>(static_cast<const uint8_t*>(w->packed),
-                                                                    W_out, w->E, w->K, w->N);
-    else
-        dequant_kernel<<<2048, 256, 0, (cudaStream_t)stream>>>(
-            static_cast<const uint8_t*>(w->packed), static_cast<const __half*>(w->scales),
-            static_cast<const uint32_t*>(w->zeros), W_out, w->E, w->K, w->N, layout_group(w), w->bits,
-            w->asym);
+    dequant_kernel<<<2048, 256, 0, (cudaStream_t)stream>>>(
+        static_cast<const uint8_t*>(w->packed), static_cast<const __half*>(w->scales),
+        static_cast<const uint32_t*>(w->zeros), W_out, w->E, w->K, w->N, layout_group(w), w->bits,
+        w->asym);
     CKL_CUDA_TRY(cudaGetLastError());
     return CKL_OK;
 }
@@ -832,8 +738,7 @@ size_t ckl_moe_gemm_workspace_size(const ckl_moe_weights* w, int A, int swiglu, 
     const DeviceInfo* di = device_info();
     if (!di) return 0;
     const int ks = force_ksplit > 0 ? std::min(force_ksplit, w->K / KGROUP_STAGE)
-                   : w->layout == CKL_MOE_LAYOUT_COLUMN ? col_gemm_ksplit(di, w, A)
-                                                         : pick_ksplit(di, num_quads(w->N), std::min(w->E, A), w->K);
+                                    : pick_ksplit(di, num_quads(w->N), std::min(w->E, A), w->K);
     if (ks <= 1) return 0;
     return (size_t)ks * A * w->N * sizeof(float) * (swiglu ? 2 : 1);
 }
@@ -864,7 +769,7 @@ ckl_status expert_gemm(const void* X, const int* row_src, const int* offsets, in
         st = check_weights(w1, "moe_expert_gemm (up)");
         if (st != CKL_OK) return st;
         if (w1->bits != w0->bits || w1->E != w0->E || w1->K != w0->K || w1->N != w0->N ||
-            w1->group != w0->group || w1->asym != w0->asym || w1->layout != w0->layout)
+            w1->group != w0->group || w1->asym != w0->asym)
             return fail(CKL_INVALID_ARG, "moe_expert_gemm: gate/up weights differ in format");
     }
     if (A < 0) return fail(CKL_INVALID_ARG, "moe_expert_gemm: A < 0");
@@ -877,20 +782,12 @@ ckl_status expert_gemm(const void* X, const int* row_src, const int* offsets, in
     if (st != CKL_OK) return st;
     const int quads = num_quads(w0->N);
     const int slots = std::min(w0->E, A);
-    const bool column = w0->layout == CKL_MOE_LAYOUT_COLUMN;
     const int ks = force_ksplit > 0 ? std::min(force_ksplit, w0->K / KGROUP_STAGE)
-                   : column ? col_gemm_ksplit(di, w0, A) : pick_ksplit(di, quads, slots, w0->K);
+                                    : pick_ksplit(di, quads, slots, w0->K);
     const size_t need = ks > 1 ? (size_t)ks * A * w0->N * sizeof(float) * (swiglu ? 2 : 1) : 0;
     if (ks > 1 && (!workspace || workspace_bytes < need))
         return fail(CKL_WORKSPACE_TOO_SMALL, "moe_expert_gemm needs %zu workspace bytes, got %zu",
                     need, workspace_bytes);
-    const cudaStream_t s = (cudaStream_t)stream;
-    if (column) {
-        st = expert_gemm_col(X, row_src, offsets, A, w0, w1, Y, y_f32, ks, workspace, dep, row_dst, s);
-        if (st != CKL_OK) return st;
-        return ks > 1 ? splitk_reduce(workspace, Y, y_f32, A, w0->N, ks, swiglu, row_dst, a_rows, dep, s)
-                      : CKL_OK;
-    }
     const bool grouped = embeds_params(w0->bits, w0->group);   // int4, or int8 group 128
     (void)max_rows;   // passes of up to 16 rows; the tile count is chosen per pass on the device
     GemmArgs a;
@@ -915,9 +812,17 @@ ckl_status expert_gemm(const void* X, const int* row_src, const int* offsets, in
     void* args[] = {&a};
     const Variant v = gemm_variant(w0->bits, swiglu, grouped);
     dim3 grid((unsigned)quads, (unsigned)slots, (unsigned)ks);
+    const cudaStream_t s = (cudaStream_t)stream;
     CKL_CUDA_TRY(launch(v.fn, grid, dim3(GTHREADS), v.smem, s, args, dep != 0));
-    return ks > 1 ? splitk_reduce(workspace, Y, y_f32, A, w0->N, ks, swiglu, row_dst, a_rows, dep, s)
-                  : CKL_OK;
+    if (ks > 1) {
+        const float* P = static_cast<const float*>(workspace);
+        int ksv = ks, Av = A, Nv = w0->N;
+        void* rargs[] = {&P, &Y, &y_f32, &Av, &Nv, &ksv, &row_dst, &a_rows};
+        const void* rfn = swiglu ? reinterpret_cast<const void*>(splitk_reduce_kernel<true>)
+                                 : reinterpret_cast<const void*>(splitk_reduce_kernel<false>);
+        CKL_CUDA_TRY(launch(rfn, dim3(256), dim3(256), 0, s, rargs, dep != 0));
+    }
+    return CKL_OK;
 }
 
 }  // namespace moe

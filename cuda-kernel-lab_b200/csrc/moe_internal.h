@@ -17,13 +17,6 @@ ckl_status expert_gemm(const void* X, const int* row_src, const int* offsets, in
                        int force_ksplit, void* workspace, size_t workspace_bytes, void* stream,
                        int dep = 0, const int* row_dst = nullptr, const int* a_rows = nullptr);
 
-// The column-layout path (moe_gemm_col.cu, tcgen05 with A in tensor memory): its split-K
-// factor for A rows, and its launch (ks > 1 writes fp32 partials to workspace).
-int col_gemm_ksplit(const DeviceInfo* di, const ckl_moe_weights* w, int A);
-ckl_status expert_gemm_col(const void* X, const int* row_src, const int* offsets, int A,
-                           const ckl_moe_weights* w0, const ckl_moe_weights* w1, void* Y, int y_f32,
-                           int ks, void* workspace, int dep, const int* row_dst, cudaStream_t s);
-
 // Routing of T tokens: ids, wts, counts, offsets, inv_perm and row_src (the token of each
 // expert-sorted row).
 ckl_status route_tokens(const float* logits, int T, int E, int k, int* ids, float* wts,

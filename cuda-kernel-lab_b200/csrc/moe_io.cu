@@ -7,7 +7,7 @@
 //
 //   offset  size  field (little-endian)
 //   0       8     magic "CKLMOEW1"
-//   8       4     format version: the packed layout (1 fragment, 2 column)
+//   8       4     format version (1)
 //   12      4     bits (4, 8, 16)
 //   16      4     E
 //   20      4     K
@@ -20,8 +20,7 @@
 //   56      8     zero-point words (uint32; 0 unless asym)
 //   64      ...   payload: packed codes, scales, zero points
 //
-// The packed layouts are described in moe_common.cuh: version 1 is the fragment layout,
-// version 2 the column layout (CKL_MOE_LAYOUT_COLUMN).
+// The packed layout itself is described in moe_common.cuh; version 1 is that layout.
 
 #include <cstdio>
 #include <cstring>
@@ -33,7 +32,7 @@ namespace ckl {
 namespace moeio {
 
 constexpr char MAGIC[8] = {'C', 'K', 'L', 'M', 'O', 'E', 'W', '1'};
-constexpr uint32_t VERSION_MIN = 1, VERSION_MAX = 2;   // = 1 + layout
+constexpr uint32_t VERSION = 1;
 constexpr size_t HEADER = 64;
 
 struct Header {
@@ -64,7 +63,7 @@ uint32_t crc32_update(uint32_t crc, const uint8_t* p, size_t n) {
 // Byte sizes of the three buffers for a weights description.
 void sizes(const ckl_moe_weights* w, uint64_t* packed, uint64_t* scales, uint64_t* zeros) {
     const int group = w->bits == 16 ? w->K : w->group;
-    *packed = ckl_moe_packed_bytes_layout(w->bits, w->E, w->K, w->N, group, w->layout);
+    *packed = ckl_moe_packed_bytes(w->bits, w->E, w->K, w->N, group);
     *scales = w->bits == 16 ? 0 : ckl_moe_scale_count(w->E, w->K, w->N, group);
     *zeros = w->asym ? ckl_moe_zero_words(w->E, w->K, w->N, group) : 0;
 }
@@ -72,12 +71,11 @@ void sizes(const ckl_moe_weights* w, uint64_t* packed, uint64_t* scales, uint64_
 ckl_status read_header(FILE* f, const char* path, Header* h) {
     if (fread(h, 1, HEADER, f) != HEADER) return fail(CKL_INVALID_ARG, "%s: short header", path);
     if (memcmp(h->magic, MAGIC, 8) != 0) return fail(CKL_INVALID_ARG, "%s: not a packed-weights file", path);
-    if (h->version < VERSION_MIN || h->version > VERSION_MAX)
-        return fail(CKL_UNSUPPORTED_SHAPE, "%s: format version %u (this library reads %u-%u)", path, h->version,
-                    VERSION_MIN, VERSION_MAX);
+    if (h->version != VERSION)
+        return fail(CKL_UNSUPPORTED_SHAPE, "%s: format version %u (this library reads %u)", path, h->version,
+                    VERSION);
     ckl_moe_weights w{};
     w.bits = h->bits; w.E = h->E; w.K = h->K; w.N = h->N; w.group = h->group; w.asym = h->asym;
-    w.layout = (int)h->version - 1;
     uint64_t p, s, z;
     sizes(&w, &p, &s, &z);
     if (p == 0 || p != h->packed || s != h->scales || z != h->zeros)
@@ -97,9 +95,7 @@ ckl_status ckl_moe_weights_save(const char* path, const ckl_moe_weights* w, void
     if (!path || !w || !w->packed) return fail(CKL_INVALID_ARG, "moe_weights_save: NULL argument");
     Header h{};
     memcpy(h.magic, MAGIC, 8);
-    if (w->layout != CKL_MOE_LAYOUT_FRAGMENT && w->layout != CKL_MOE_LAYOUT_COLUMN)
-        return fail(CKL_INVALID_ARG, "moe_weights_save: layout=%d", w->layout);
-    h.version = 1 + (uint32_t)w->layout;
+    h.version = VERSION;
     h.bits = w->bits; h.E = w->E; h.K = w->K; h.N = w->N;
     h.group = w->bits == 16 ? w->K : w->group;
     h.asym = w->asym;
@@ -134,7 +130,6 @@ ckl_status ckl_moe_weights_file_info(const char* path, ckl_moe_weights* w) {
     if (st != CKL_OK) return st;
     memset(w, 0, sizeof(*w));
     w->bits = h.bits; w->E = h.E; w->K = h.K; w->N = h.N; w->group = h.group; w->asym = h.asym;
-    w->layout = (int)h.version - 1;
     return CKL_OK;
 }
 
@@ -149,11 +144,10 @@ ckl_status ckl_moe_weights_load(const char* path, ckl_moe_weights* w, void* stre
         return st;
     }
     if (w->bits != h.bits || w->E != h.E || w->K != h.K || w->N != h.N || w->asym != h.asym ||
-        (h.bits != 16 && w->group != h.group) || w->layout != (int)h.version - 1) {
+        (h.bits != 16 && w->group != h.group)) {
         fclose(f);
-        return fail(CKL_INVALID_ARG,
-                    "moe_weights_load: %s holds bits=%d E=%d K=%d N=%d group=%d asym=%d layout=%d", path,
-                    h.bits, h.E, h.K, h.N, h.group, h.asym, (int)h.version - 1);
+        return fail(CKL_INVALID_ARG, "moe_weights_load: %s holds bits=%d E=%d K=%d N=%d group=%d asym=%d",
+                    path, h.bits, h.E, h.K, h.N, h.group, h.asym);
     }
     if ((h.scales && !w->scales) || (h.zeros && !w->zeros)) {
         fclose(f);

@@ -291,23 +291,13 @@ typedef struct ckl_moe_weights {
     int E, K, N;
     int group;
     int asym;
-    int layout;    /* CKL_MOE_LAYOUT_FRAGMENT (0, every format) or CKL_MOE_LAYOUT_COLUMN */
     void* packed;
     void* scales;
     void* zeros;
 } ckl_moe_weights;
 
-/* Packed layouts. FRAGMENT: per 16-column strip and 128-k group, each lane's mma.sync A
- * fragment (the warp-level tensor-core GEMM). COLUMN: int4 with group 128 and N % 128 == 0
- * only; per 128-column tile and group, each output column's 128 codes in k order for one
- * thread (the tcgen05 GEMM with its A operand in tensor memory). */
-#define CKL_MOE_LAYOUT_FRAGMENT 0
-#define CKL_MOE_LAYOUT_COLUMN 1
-
 /* Sizes of the three buffers of ckl_moe_weights (bytes; fp16 elements; uint32 words). */
 CKL_API size_t ckl_moe_packed_bytes(int bits, int E, int K, int N, int group);
-/* Packed bytes in a given layout (0 if the layout does not take the format). */
-CKL_API size_t ckl_moe_packed_bytes_layout(int bits, int E, int K, int N, int group, int layout);
 CKL_API size_t ckl_moe_scale_count(int E, int K, int N, int group);
 CKL_API size_t ckl_moe_zero_words(int E, int K, int N, int group);
 

@@ -111,13 +111,12 @@ def test_packed_weights_file_header(ckl, tmp_path):
     ckl.check(ckl.lib().ckl_moe_weights_file_info(str(f).encode(), C.byref(w)), "info")
     assert (w.bits, w.E, w.K, w.N, w.group, w.asym) == (4, 2, 256, 128, 128, 1)
     assert w.packed is None and w.scales is None
-    for bad in (_weights_header(magic=b"CKLMOEW0")[0], _weights_header(version=3)[0],
-                _weights_header(version=2)[0],           # column layout: other section sizes
+    for bad in (_weights_header(magic=b"CKLMOEW0")[0], _weights_header(version=2)[0],
                 _weights_header(sizes=(p + 16, s, z))[0]):
         g = tmp_path / "bad.bin"
         g.write_bytes(bad + bytes(p + 2 * s + 4 * z))
         assert ckl.lib().ckl_moe_weights_file_info(str(g).encode(), C.byref(w)) != 0
     # checksum of an all-zero payload is not 0: the load stops at the check
-    w2 = ckl.MoeWeights(4, 2, 256, 128, 128, 1, 0, 0x1000, 0x2000, 0x3000)
+    w2 = ckl.MoeWeights(4, 2, 256, 128, 128, 1, 0x1000, 0x2000, 0x3000)
     st = ckl.lib().ckl_moe_weights_load(str(f).encode(), C.byref(w2), None)
     assert st == 1 and b"checksum" in ckl.lib().ckl_last_error_string()

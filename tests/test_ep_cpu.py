@@ -165,7 +165,7 @@ def test_ep_window_layout_and_argument_checks(ckl):
     assert ckl.ep_window_bytes(9, 64, 6, 72, 2048) == 0            # world > 8
     lib = ckl.lib()
     comm = ckl.MoeEpComm(0, 2, 4, 2, 8, 256)
-    w = ckl.MoeWeights(4, 4, 256, 256, 128, 1, 0, None, None, None)
+    w = ckl.MoeWeights(4, 4, 256, 256, 128, 1, None, None, None)
     args = (None, None, 1, C.byref(w), C.byref(w), C.byref(w), None, None, None, None, 0, None)
     assert lib.ckl_moe_ep_layer(C.byref(comm), *args) == 1         # NULL windows
     comm.windows[0], comm.windows[1] = 0x10000, 0x20000

@@ -54,26 +54,6 @@ def test_quantizer_bit_exact(ckl, oracle, dev, bits, group, asym):
         assert np.array_equal(nib.astype(np.uint8), zeros)
 
 
-@pytest.mark.parametrize("asym", [False, True])
-def test_column_layout_dequant_bit_exact(ckl, oracle, dev, asym):
-    """The column layout (int4, group 128, N % 128 == 0) decodes to the same weights as the
-    host restatement of the quantiser, bit for bit, from its own embedded scales and zeros."""
-    E, K, N = 3, 384, 256
-    W = oracle.normal((E, K, N), seed=9, std=0.02)
-    q = ckl.QuantWeights(4, T_(W, dev), group=128, asym=asym, layout=ckl.LAYOUT_COLUMN)
-    got = q.dequant().cpu().numpy()
-    if asym:
-        codes, scales, zeros = oracle.quant_asym4(W)
-    else:
-        codes, scales = oracle.quant_sym(W, 4, group=128)
-        zeros = None
-    want = oracle.dequant(codes, scales, zeros, 4, group=128)
-    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
-    import torch
-    frag = ckl.QuantWeights(4, T_(W, dev), group=128, asym=asym)
-    assert torch.equal(frag.dequant(), q.dequant())
-
-
 @pytest.mark.skipif(not os.path.exists(REF03), reason="reference not compiled here")
 @pytest.mark.parametrize("bits", [4, 8, 16])
 def test_packing_matches_reference_pack_weights(ckl, oracle, dev, bits):
@@ -193,12 +173,10 @@ def test_expert_gemm_reference_case(ckl, oracle, dev, bits, ks):
     assert np.all(np.abs(got - ref) <= 2e-3 + 1e-2 * np.abs(ref))
 
 
-@pytest.mark.parametrize("layout", [0, 1])
 @pytest.mark.parametrize("asym", [True, False])
 @pytest.mark.parametrize("ks", [1, 2, 4])
-def test_expert_gemm_int4_tile_multiple_width(ckl, oracle, dev, asym, ks, layout):
-    """int4 at a width of whole 128-column tiles, in both packed layouts (fragment: mma.sync;
-    column: tcgen05 with A in tensor memory): the reference case's generators at d=1024,
+def test_expert_gemm_int4_tile_multiple_width(ckl, oracle, dev, asym, ks):
+    """int4 at a width of whole 64-column quads: the reference case's generators at d=1024,
     f=384, T=40, E=8, top-2 -- experts with more than 16 rows run in several passes, expert
     3 is empty -- K split 1, 2 and 4 ways, asymmetric and symmetric codes."""
     T, E, k, d, f = 40, 8, 2, 1024, 384
@@ -208,7 +186,7 @@ def test_expert_gemm_int4_tile_multiple_width(ckl, oracle, dev, asym, ks, layout
     r = ckl.route_and_permute(T_(lg, dev), T_(X, dev), k)
     offs = r["offsets"].cpu().numpy()
     assert offs[4] == offs[3] and np.diff(offs).max() > 16
-    q = ckl.QuantWeights(4, T_(W, dev), group=128, asym=asym, layout=layout)
+    q = ckl.QuantWeights(4, T_(W, dev), group=128, asym=asym)
     import torch
     Yp = torch.zeros((T * k, f), dtype=torch.float16, device=dev)
     q.run(r["Xp"], Yp, r["offsets"], T * k, force_ksplit=ks)
@@ -226,17 +204,14 @@ def _layer_weights(ckl, oracle, dev, E, d, F, mode, seed=11):
     Wu = oracle.normal((E, d, F), seed=seed + 1, std=0.02)
     Wd = oracle.normal((E, F, d), seed=seed + 2, std=0.02)
     kw = dict(int4=dict(bits=4, group=128, asym=True), int8pc=dict(bits=8, group=0),
-              fp16=dict(bits=16, group=0), int4sym=dict(bits=4, group=128),
-              int4col=dict(bits=4, group=128, asym=True, layout=1),
-              int4symcol=dict(bits=4, group=128, layout=1))[mode]
+              fp16=dict(bits=16, group=0), int4sym=dict(bits=4, group=128))[mode]
     def q(W):
         g = kw.get("group") or W.shape[1]
-        return ckl.QuantWeights(kw["bits"], T_(W, dev), group=g, asym=kw.get("asym", False),
-                                layout=kw.get("layout", 0))
+        return ckl.QuantWeights(kw["bits"], T_(W, dev), group=g, asym=kw.get("asym", False))
     return q(Wg), q(Wu), q(Wd)
 
 
-@pytest.mark.parametrize("mode", ["int4", "int8pc", "fp16", "int4sym", "int4col", "int4symcol"])
+@pytest.mark.parametrize("mode", ["int4", "int8pc", "fp16", "int4sym"])
 @pytest.mark.parametrize("T", [1, 5, 33])
 def test_moe_layer_against_fp64_oracle(ckl, oracle, dev, mode, T):
     import torch
@@ -275,19 +250,18 @@ def _torch_layer_ref(X, ids, wts, Wg, Wu, Wd):
     return out
 
 
-@pytest.mark.parametrize("layout", [0, 1])
 @pytest.mark.parametrize("T", [1, 4, 16, 64])
-def test_config4_w4a16_layer_full_size(ckl, oracle, dev, T, layout):
+def test_config4_w4a16_layer_full_size(ckl, oracle, dev, T):
     """E=64, top-6, d=2048, F=1408, asymmetric int4 g128, weights
-    N(0,0.02), activations and logits N(0,1); both packed layouts."""
+    N(0,0.02), activations and logits N(0,1)."""
     import torch
     E, k, d, F = 64, 6, 2048, 1408
     g = torch.Generator(device=dev)
     g.manual_seed(4)
     mk = lambda *s: (torch.randn(*s, generator=g, device=dev) * 0.02).half()
-    gq = ckl.QuantWeights(4, mk(E, d, F), group=128, asym=True, layout=layout)
-    uq = ckl.QuantWeights(4, mk(E, d, F), group=128, asym=True, layout=layout)
-    dq = ckl.QuantWeights(4, mk(E, F, d), group=128, asym=True, layout=layout)
+    gq = ckl.QuantWeights(4, mk(E, d, F), group=128, asym=True)
+    uq = ckl.QuantWeights(4, mk(E, d, F), group=128, asym=True)
+    dq = ckl.QuantWeights(4, mk(E, F, d), group=128, asym=True)
     lg = torch.randn((T, E), generator=g, device=dev)
     X = torch.randn((T, d), generator=g, device=dev).half()
     ids = torch.empty((T, k), dtype=torch.int32, device=dev)
@@ -325,7 +299,7 @@ def test_config5_w8a16_moe_full_size(ckl, oracle, dev):
     torch.cuda.empty_cache()
 
 
-@pytest.mark.parametrize("mode", ["int4", "int8pc", "fp16", "int4sym", "int4col"])
+@pytest.mark.parametrize("mode", ["int4", "int8pc", "fp16", "int4sym"])
 def test_packed_weights_file_round_trip(ckl, oracle, dev, tmp_path, mode):
     """ckl_moe_weights_save / _file_info / _load: the buffers come back bit for bit and the
     layer computes the same output from the loaded weights."""
@@ -337,8 +311,7 @@ def test_packed_weights_file_round_trip(ckl, oracle, dev, tmp_path, mode):
         q.save(pth)
     lq = [ckl.QuantWeights.load(pth, device=dev) for pth in paths]
     for a, b in zip((gq, uq, dq), lq):
-        assert (a.bits, a.E, a.K, a.N, a.group, a.asym, a.layout) == (b.bits, b.E, b.K, b.N, b.group,
-                                                                       b.asym, b.layout)
+        assert (a.bits, a.E, a.K, a.N, a.group, a.asym) == (b.bits, b.E, b.K, b.N, b.group, b.asym)
         assert torch.equal(a.packed, b.packed)
         if a.bits != 16:
             assert torch.equal(a.scales, b.scales)
