@@ -37,7 +37,9 @@ constexpr int TILES = 4;                     // 16-column tiles per CTA (a 64-co
 constexpr int GPS = 2;                       // 128-k groups per pipeline stage
 constexpr int CONSUMERS = TILES * GPS;       // warp w: tile w % 4, group (w / 4) of the stage
 constexpr int GTHREADS = (CONSUMERS + 1) * 32;
-constexpr int RING_BYTES = 96 * 1024;
+// Shared-memory ring per CTA at OCC resident CTAs per SM: 2 (deep ring, for grids of at most
+// one wave) or 3 (more warps to hide latency, for larger grids).
+constexpr int ring_bytes(int occ) { return occ == 3 ? 64 * 1024 : 96 * 1024; }
 constexpr int XSTRIDE = GPS * 256 + 64;      // smem bytes per staged token row (pad: the two
                                              // rows a quarter-warp reads land on disjoint banks)
 constexpr int MAX_STAGES = 16;
@@ -118,7 +120,7 @@ __device__ __forceinline__ int nth_active_expert(const int* offsets, int E, int 
     return -1;
 }
 
-template <int BITS, bool SWIGLU, bool GROUPED>
+template <int BITS, bool SWIGLU, bool GROUPED, int OCC>
 struct Cfg {
     static constexpr int MATS = SWIGLU ? 2 : 1;
     static constexpr bool EMBED = embeds_params(BITS, GROUPED ? KGROUP_STAGE : 0);
@@ -128,7 +130,7 @@ struct Cfg {
     static constexpr int WBYTES = MATS * GPS * GBLK;               // weights per stage
     static constexpr int XROWS = TMAX * 8;
     static constexpr int SBYTES = (WBYTES + XROWS * XSTRIDE + 127) / 128 * 128;
-    static constexpr int STAGES_RAW = RING_BYTES / SBYTES;
+    static constexpr int STAGES_RAW = ring_bytes(OCC) / SBYTES;
     static constexpr int STAGES = STAGES_RAW > MAX_STAGES ? MAX_STAGES : STAGES_RAW;
     static constexpr int RVALS = TMAX * 4 * MATS;                  // fp32 values per lane
     static constexpr int RED = TILES * 32 * RVALS * 4;              // cross-warp reduction
@@ -136,12 +138,12 @@ struct Cfg {
 };
 
 // Consumer pass over all stages for `NT` token tiles; returns false on a timeout.
-template <int BITS, bool SWIGLU, bool GROUPED, int NT>
+template <int BITS, bool SWIGLU, bool GROUPED, int OCC, int NT>
 __device__ __forceinline__ bool consume_pass(const GemmArgs& a, const uint8_t* ring, uint64_t* full,
                                              uint64_t* empty, int& seq, int nst, int g_beg,
                                              int g_end, uint64_t deadline,
                                              float (&acc0)[TMAX][4], float (&acc1)[TMAX][4]) {
-    using C = Cfg<BITS, SWIGLU, GROUPED>;
+    using C = Cfg<BITS, SWIGLU, GROUPED, OCC>;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
     const int tile = warp % TILES, half = warp / TILES;
     constexpr int SPC = 16 / bytes_per_lane(BITS);         // k16 steps per 16-byte lane chunk
@@ -239,10 +241,10 @@ __device__ __forceinline__ void consumer_bar() {
 }
 
 // grid = (quads, min(E, A) expert slots, ksplit); 9 warps (8 consumers + 1 producer).
-template <int BITS, bool SWIGLU, bool GROUPED>
-__global__ void __launch_bounds__(GTHREADS, 2)
+template <int BITS, bool SWIGLU, bool GROUPED, int OCC>
+__global__ void __launch_bounds__(GTHREADS, OCC)
 moe_gemm_kernel(const GemmArgs a) {
-    using C = Cfg<BITS, SWIGLU, GROUPED>;
+    using C = Cfg<BITS, SWIGLU, GROUPED, OCC>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* ring = align_ptr<128>(smem_raw);
     float* red = reinterpret_cast<float*>(ring + C::STAGES * C::SBYTES);
@@ -366,8 +368,8 @@ moe_gemm_kernel(const GemmArgs a) {
 #pragma unroll
             for (int c = 0; c < 4; c++) acc0[i][c] = acc1[i][c] = 0.f;
         const bool ok = ntl == 1
-            ? consume_pass<BITS, SWIGLU, GROUPED, 1>(a, ring, full, empty, seq, nst, g_beg, g_end, deadline, acc0, acc1)
-            : consume_pass<BITS, SWIGLU, GROUPED, TMAX>(a, ring, full, empty, seq, nst, g_beg, g_end, deadline, acc0, acc1);
+            ? consume_pass<BITS, SWIGLU, GROUPED, OCC, 1>(a, ring, full, empty, seq, nst, g_beg, g_end, deadline, acc0, acc1)
+            : consume_pass<BITS, SWIGLU, GROUPED, OCC, TMAX>(a, ring, full, empty, seq, nst, g_beg, g_end, deadline, acc0, acc1);
         if (!__all_sync(0xffffffffu, ok)) return;          // timed out (already recorded)
 
         // the two warps of a tile hold partial sums over alternate groups: add them
@@ -616,17 +618,22 @@ struct Variant {
     KernelFn fn;
     int smem;
 };
-Variant gemm_variant(int bits, bool swiglu, bool grouped) {
-#define CKL_V(B, SW, GR) \
-    Variant{reinterpret_cast<KernelFn>(moe_gemm_kernel<B, SW, GR>), Cfg<B, SW, GR>::SMEM}
-    if (bits == 4) return swiglu ? CKL_V(4, true, true) : CKL_V(4, false, true);
+#define CKL_V(B, SW, GR, OCC) \
+    Variant{reinterpret_cast<KernelFn>(moe_gemm_kernel<B, SW, GR, OCC>), Cfg<B, SW, GR, OCC>::SMEM}
+// 3 CTAs per SM only for int4 (its stages fit twice in 64 KB; measured faster past one wave
+// of 2). The int8 and fp16 stages are 1.6-2.4x larger: at 64 KB a ring would hold one stage.
+Variant gemm_variant(int bits, bool swiglu, bool grouped, int occ) {
+    if (bits == 4)
+        return occ == 3 ? (swiglu ? CKL_V(4, true, true, 3) : CKL_V(4, false, true, 3))
+                        : (swiglu ? CKL_V(4, true, true, 2) : CKL_V(4, false, true, 2));
     if (bits == 8) {
-        if (grouped) return swiglu ? CKL_V(8, true, true) : CKL_V(8, false, true);
-        return swiglu ? CKL_V(8, true, false) : CKL_V(8, false, false);
+        if (grouped) return swiglu ? CKL_V(8, true, true, 2) : CKL_V(8, false, true, 2);
+        return swiglu ? CKL_V(8, true, false, 2) : CKL_V(8, false, false, 2);
     }
-    return swiglu ? CKL_V(16, true, false) : CKL_V(16, false, false);
-#undef CKL_V
+    return swiglu ? CKL_V(16, true, false, 2) : CKL_V(16, false, false, 2);
 }
+#undef CKL_V
+bool gemm_occ3(int bits) { return bits == 4; }
 
 ckl_status gemm_setup(const DeviceInfo* di) {
     static ckl_status st[64];
@@ -634,9 +641,11 @@ ckl_status gemm_setup(const DeviceInfo* di) {
     std::call_once(once[di->device], [di] {
         st[di->device] = CKL_OK;
         for (int bits : {4, 8, 16})
+            for (int occ : {2, 3})
             for (int sw = 0; sw < 2; sw++)
                 for (int gr = 0; gr < 2; gr++) {
-                    const Variant v = gemm_variant(bits, sw, gr);
+                    if (occ == 3 && !gemm_occ3(bits)) continue;
+                    const Variant v = gemm_variant(bits, sw, gr, occ);
                     cudaError_t e = cudaFuncSetAttribute(
                         v.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, v.smem);
                     if (e != cudaSuccess) {
@@ -810,7 +819,10 @@ ckl_status expert_gemm(const void* X, const int* row_src, const int* offsets, in
     a.y_f32 = y_f32;
     a.dep = dep;
     void* args[] = {&a};
-    const Variant v = gemm_variant(w0->bits, swiglu, grouped);
+    // 3 CTAs per SM (64 KB rings) when the grid is more than one wave of 2 (int4), else the
+    // deeper rings of 2 CTAs per SM
+    const int occ = gemm_occ3(w0->bits) && (long long)quads * slots * ks > 2LL * di->sms ? 3 : 2;
+    const Variant v = gemm_variant(w0->bits, swiglu, grouped, occ);
     dim3 grid((unsigned)quads, (unsigned)slots, (unsigned)ks);
     const cudaStream_t s = (cudaStream_t)stream;
     CKL_CUDA_TRY(launch(v.fn, grid, dim3(GTHREADS), v.smem, s, args, dep != 0));
