@@ -245,6 +245,19 @@ def committed_traffic(kernel, workload):
 
 
 # ------------------------------------------------------------------ CPU baselines
+def cpu_model():
+    """The host CPU's model string (/proc/cpuinfo), or the platform's processor name."""
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    import platform
+    return platform.processor() or "unknown"
+
+
 def cpu_baseline_sample(L, threads, min_seqs=64):
     """The reference's cpu_reference (oracle/_ref) on `threads` threads over a bounded
     sample of ~min_seqs sequences of length L; returns the cpu_baseline object."""
@@ -260,13 +273,14 @@ def cpu_baseline_sample(L, threads, min_seqs=64):
         nseq = threads * bpt
         byts = kvb + nseq * HQ * D * 2 * 2 + nseq * HQ * 4
         return {"value": byts / sec / 1e9, "unit": "GB/s", "cores": threads, "kind": "reference",
+                "cpu_model": cpu_model(),
                 "sample": f"{nseq} sequences x L={L} (Hq={HQ}, Hkv={HKV}), {threads} threads x "
                           f"{bpt}; cpu_reference 01_decode_attention.cu:371-400 compiled from "
                           f"the reference sources; {sec:.2f} s"}
     bt = O.batch([L] * 8, HQ, HKV, 11)
     sec = O.port_attention_seconds(bt, threads)
     return {"value": algorithmic_bytes([L] * 8) / sec / 1e9, "unit": "GB/s", "cores": threads,
-            "kind": "port", "sample": f"8 sequences x L={L}, oracle port, {sec:.2f} s"}
+            "kind": "port", "cpu_model": cpu_model(), "sample": f"8 sequences x L={L}, oracle port, {sec:.2f} s"}
 
 
 def run_reference(args):
@@ -303,6 +317,7 @@ def run_reference(args):
             "vs_baseline": None, "dtype": "f64", "data": "synthetic (reference generator)",
             "config": config_of(args.workload, lens, args.gpus),
             "cpu_baseline": {"value": val, "unit": "GB/s", "cores": threads, "kind": "reference",
+                             "cpu_model": cpu_model(),
                              "sample": f"per step {nseq} sequences x L={L} (one per thread) of "
                                        "the workload; cpu_reference compiled from the reference"},
             "e2e": {"value": val, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}

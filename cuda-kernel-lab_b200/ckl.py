@@ -4,6 +4,10 @@ Every call goes through libckl.so (include/ckl.h); there is no CPU or PyTorch fa
 if the library is missing or a call fails, a CklError is raised. PyTorch is used only as
 plumbing -- device tensors, streams -- and tensors cross the boundary as raw pointers.
 
+This module is the mirror the tests and bench.py drive the library through; it needs torch
+to allocate buffers. libckl.so itself does not depend on torch: its C ABI takes plain
+device pointers, sizes and a cudaStream_t, and a C/C++ host calls it directly.
+
 Names follow the reference (01_decode_attention.cu, 03_moe_wq_decode.cu, common/moe.cuh):
 plan_chunks, decode_attention, merge_states, shared_prefix_pages, plan_cascade,
 cascade_decode, ...
@@ -129,6 +133,8 @@ _SIGS = {
     "ckl_moe_zero_words": (C.c_size_t, [C.c_int, C.c_int, C.c_int, C.c_int]),
     "ckl_moe_pack_weights": (C.c_int, [C.c_void_p, C.POINTER(MoeWeights), C.c_void_p]),
     "ckl_moe_dequant_weights": (C.c_int, [C.POINTER(MoeWeights), C.c_void_p, C.c_void_p]),
+    "ckl_moe_import_reference_packed": (C.c_int, [C.c_void_p, C.c_void_p, C.POINTER(MoeWeights),
+                                                  C.c_void_p]),
     "ckl_moe_gemm_workspace_size": (C.c_size_t, [C.POINTER(MoeWeights), C.c_int, C.c_int,
                                                  C.c_int]),
     "ckl_moe_expert_gemm": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int,
@@ -524,6 +530,29 @@ class QuantWeights:
         check(L.ckl_moe_pack_weights(_ptr(W), C.byref(self.w), _stream(stream)),
               "ckl_moe_pack_weights")
 
+    @classmethod
+    def from_reference_packed(cls, bits, P, Sc, E, K, N, stream=None):
+        """Weights the reference's QuantWeights packed (P uint32 words in widx order and
+        Sc fp16 [E][K/128][N], 03_moe_wq_decode.cu:43-87), re-laid on the device
+        (ckl_moe_import_reference_packed). P and Sc are CUDA tensors."""
+        torch = _torch()
+        group = K if bits == 16 else 128
+        self = cls.__new__(cls)
+        self.bits, self.E, self.K, self.N, self.group, self.asym = bits, E, K, N, group, False
+        L = lib()
+        dev = P.device
+        self.packed = torch.empty(L.ckl_moe_packed_bytes(bits, E, K, N, group), dtype=torch.uint8,
+                                  device=dev)
+        ns = L.ckl_moe_scale_count(E, K, N, group) if bits != 16 else 1
+        self.scales = torch.empty(max(ns, 1), dtype=torch.float16, device=dev)
+        self.zeros = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.w = MoeWeights(bits, E, K, N, group, 0, self.packed.data_ptr(),
+                            self.scales.data_ptr() if bits != 16 else None, None)
+        check(L.ckl_moe_import_reference_packed(_ptr(P), _ptr(Sc) if bits != 16 else None,
+                                                C.byref(self.w), _stream(stream)),
+              "ckl_moe_import_reference_packed")
+        return self
+
     def dequant(self, stream=None):
         torch = _torch()
         out = torch.empty((self.E, self.K, self.N), dtype=torch.float32, device=self.packed.device)
@@ -560,6 +589,26 @@ class QuantWeights:
         check(L.ckl_moe_weights_load(os.fsencode(path), C.byref(self.w), _stream(stream)),
               "ckl_moe_weights_load")
         return self
+
+    def expert(self, e):
+        """Expert e alone (E=1), a view sharing this object's device buffers: the packed
+        codes, the scales and the zero points are all laid out expert-major."""
+        L = lib()
+        v = QuantWeights.__new__(QuantWeights)
+        v.bits, v.E, v.K, v.N, v.group, v.asym = self.bits, 1, self.K, self.N, self.group, self.asym
+        pb = L.ckl_moe_packed_bytes(self.bits, 1, self.K, self.N, self.group)
+        v.packed = self.packed[e * pb:(e + 1) * pb]
+        v.scales, v.zeros = self.scales, self.zeros
+        if self.bits != 16:
+            ns = L.ckl_moe_scale_count(1, self.K, self.N, self.group)
+            v.scales = self.scales[e * ns:(e + 1) * ns]
+        if self.asym:
+            nz = L.ckl_moe_zero_words(1, self.K, self.N, self.group)
+            v.zeros = self.zeros[e * nz:(e + 1) * nz]
+        v.w = MoeWeights(v.bits, 1, v.K, v.N, v.group, int(v.asym), v.packed.data_ptr(),
+                         v.scales.data_ptr() if v.bits != 16 else None,
+                         v.zeros.data_ptr() if v.asym else None)
+        return v
 
     def bytes_per_expert(self):
         """Algorithmic bytes of one expert: codes + scales (+ zero points), the bytes a

@@ -327,6 +327,13 @@ ckl_status validate(const ckl_decode_params* p, int* G) {
                     p->part_stride, p->chunk_base, p->num_chunks);
     if ((long long)p->B * p->Hkv > 0x7fffffffLL || p->num_chunks > 65535)
         return fail(CKL_UNSUPPORTED_SHAPE, "grid too large");
+    // partial slots per row are bounded like the chunk count, so the workspace size
+    // (B * Hq * part_stride * 516 bytes) cannot wrap and no slot index leaves the buffer
+    size_t bytes = 0;
+    if (p->part_stride > 65535 ||
+        __builtin_mul_overflow((size_t)p->B * (size_t)p->Hq, (size_t)p->part_stride * (D + 1) * sizeof(float), &bytes))
+        return fail(CKL_UNSUPPORTED_SHAPE, "part_stride=%d (at most 65535 partial slots per row)",
+                    p->part_stride);
     return CKL_OK;
 }
 
@@ -427,6 +434,10 @@ ckl_status ckl_decode_plan(int G, int B, int Hkv, int max_len, int force_chunks,
 size_t ckl_decode_workspace_size(const ckl_decode_params* p) {
     if (!p || p->B <= 0) return 0;
     if (p->num_chunks == 1 && p->chunk_base == 0 && p->part_stride == 1) return 0;
+    // shapes the launch would reject: report a size no caller can provide
+    if (p->Hq <= 0 || p->part_stride <= 0 || p->part_stride > 65535 ||
+        (long long)p->B * p->Hq > 0x7fffffffLL)
+        return SIZE_MAX;
     return part_o_bytes(p) + align_up((size_t)p->B * p->Hq * p->part_stride * sizeof(float), 256);
 }
 

@@ -23,22 +23,31 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[CKL_NOALLOC_SCR
 
 constexpr int kMaxDevices = 64;
 void* g_scratch_ptr[kMaxDevices];
-cudaError_t g_scratch_err[kMaxDevices];
-std::once_flag g_scratch_once[kMaxDevices];
+bool g_scratch_valid[kMaxDevices];
+std::mutex g_scratch_mu[kMaxDevices];
 
-// Device address of the scratch on the current device, looked up once per device while
-// that device is current.
+// Device address of the scratch on the current device. The lookup runs while that device is
+// current and its result is kept only when it succeeds: a failed lookup (for example an
+// error left behind by an earlier kernel) is retried by the next call instead of failing
+// every later call on that device. The kept address belongs to the device's primary
+// context; it does not survive cudaDeviceReset, after which this entry point must not be
+// called again in the same process.
 ckl_status scratch_on_current_device(void** out) {
     int dev = 0;
     CKL_CUDA_TRY(cudaGetDevice(&dev));
     if (dev < 0 || dev >= kMaxDevices) return fail(CKL_CUDA_ERROR, "device %d out of range", dev);
-    std::call_once(g_scratch_once[dev], [dev] {
+    std::lock_guard<std::mutex> lock(g_scratch_mu[dev]);
+    if (!g_scratch_valid[dev]) {
         void* p = nullptr;
-        g_scratch_err[dev] = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess || !p) {
+            (void)cudaGetLastError();   // do not leave the lookup's error for the next call
+            return cuda_status(e != cudaSuccess ? e : cudaErrorInvalidSymbol,
+                               "cudaGetSymbolAddress(noalloc scratch)");
+        }
         g_scratch_ptr[dev] = p;
-    });
-    if (g_scratch_err[dev] != cudaSuccess)
-        return cuda_status(g_scratch_err[dev], "cudaGetSymbolAddress(noalloc scratch)");
+        g_scratch_valid[dev] = true;
+    }
     *out = g_scratch_ptr[dev];
     return CKL_OK;
 }

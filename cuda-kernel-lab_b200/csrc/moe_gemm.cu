@@ -514,9 +514,49 @@ __device__ __forceinline__ uint8_t* record_ptr(uint8_t* P, int bits, int group, 
            (size_t)(tile % 4) * record_bytes(bits, group);
 }
 
+// Where the packer takes its codes from: quantising fp16 weights with the scales (and zero
+// points) computed by quant_params_kernel.
+struct QuantSource {
+    const __half* W;
+    const __half* S;
+    const uint32_t* Z;
+    int E, K, N, group, bits, asym;
+    __device__ uint16_t half_bits(int e, int k, int n) const {
+        return __half_as_ushort(W[((size_t)e * K + k) * N + n]);
+    }
+    __device__ uint32_t code(int e, int k, int n) const {
+        return (uint32_t)quant_code(W, S, Z, e, k, n, K, N, group, bits, asym);
+    }
+};
+
+// ... or reading them from words the reference's pack_weights<BITS> wrote
+// (03_moe_wq_decode.cu:43-87): word widx(e, k, cw) = ((e * (K/4) + k/4) * ncw + cw) * 4 + k%4
+// holds columns cw*CPT .. cw*CPT+CPT-1 (CPT = 32/bits) at bit offsets bits*c, as
+// offset-binary codes (q + 8 / q + 128) or, for bits 16, two fp16 values. The codes are
+// taken as they are: the record stores the same offset-binary codes the quantiser would
+// have produced from the same weights.
+struct RefPackedSource {
+    const uint32_t* P;
+    int K, N, bits;
+    __device__ uint32_t word(int e, int k, int n) const {
+        const int cpt = 32 / bits, ncw = N / cpt;
+        return __ldg(P + (((size_t)e * (K / 4) + k / 4) * ncw + n / cpt) * 4 + k % 4);
+    }
+    __device__ uint16_t half_bits(int e, int k, int n) const {
+        return (uint16_t)(word(e, k, n) >> (16 * (n % 2)));
+    }
+    __device__ uint32_t code(int e, int k, int n) const {
+        if (n >= N) return bits == 8 ? 128u : 8u;            // padding columns decode to 0
+        const int cpt = 32 / bits;
+        return (word(e, k, n) >> (bits * (n % cpt))) & ((1u << bits) - 1u);
+    }
+};
+
 // One thread per (e, tile, k16 step, lane): writes that lane's fragment bytes; the lane-0
-// thread of each group's first step also writes the record's embedded parameters.
-__global__ void pack_kernel(const __half* W, const __half* S, const uint32_t* Z, uint8_t* P,
+// thread of each group's first step also writes the record's embedded parameters (scales S
+// [E][K/group][N] and, for asym, zero nibbles Z, both in the reference's layout).
+template <class Src>
+__global__ void pack_kernel(Src src, const __half* S, const uint32_t* Z, uint8_t* P,
                             int E, int K, int N, int group, int bits, int asym) {
     const int steps = K / 16;
     const int ntiles = num_quads(N) * 4;
@@ -539,14 +579,14 @@ __global__ void pack_kernel(const __half* W, const __half* S, const uint32_t* Z,
             frag_coord(ks, lane, j, &k, &c);
             const int n = nt * 16 + c;
             if (bits == 16) {
-                const uint16_t h = n < N ? __half_as_ushort(W[((size_t)e * K + k) * N + n]) : 0;
+                const uint16_t h = n < N ? src.half_bits(e, k, n) : 0;
                 out[j >> 1] |= (uint32_t)h << (16 * (j & 1));
             } else if (bits == 8) {
-                const uint32_t q = (uint32_t)quant_code(W, S, Z, e, k, n, K, N, group, bits, asym);
+                const uint32_t q = src.code(e, k, n);
                 const int byte = (j >> 2) * 4 + ((j >> 1) & 1) + 2 * (j & 1);
                 out[byte >> 2] |= q << (8 * (byte & 3));
             } else {
-                const uint32_t q = (uint32_t)quant_code(W, S, Z, e, k, n, K, N, group, bits, asym);
+                const uint32_t q = src.code(e, k, n);
                 const int nib = (j >> 1) + 4 * (j & 1);
                 out[0] |= q << (4 * nib);
             }
@@ -721,11 +761,34 @@ ckl_status ckl_moe_pack_weights(const void* W, ckl_moe_weights* w, void* stream)
                                                  group, w->bits, w->asym);
         CKL_CUDA_TRY(cudaGetLastError());
     }
-    pack_kernel<<<2048, 256, 0, s>>>(static_cast<const __half*>(W),
-                                     static_cast<const __half*>(w->scales),
+    const QuantSource src{static_cast<const __half*>(W), static_cast<const __half*>(w->scales),
+                          static_cast<const uint32_t*>(w->zeros), w->E, w->K, w->N, group,
+                          w->bits, w->asym};
+    pack_kernel<<<2048, 256, 0, s>>>(src, static_cast<const __half*>(w->scales),
                                      static_cast<const uint32_t*>(w->zeros),
                                      static_cast<uint8_t*>(w->packed), w->E, w->K, w->N, group,
                                      w->bits, w->asym);
+    CKL_CUDA_TRY(cudaGetLastError());
+    return CKL_OK;
+}
+
+ckl_status ckl_moe_import_reference_packed(const uint32_t* P, const void* Sc, ckl_moe_weights* w,
+                                           void* stream) {
+    ckl_status st = check_weights(w, "moe_import_reference_packed");
+    if (st != CKL_OK) return st;
+    if (w->asym) return fail(CKL_UNSUPPORTED_SHAPE, "moe_import_reference_packed: the reference's codes are symmetric (asym must be 0)");
+    if (w->bits != 16 && w->group != KGROUP_STAGE)
+        return fail(CKL_UNSUPPORTED_SHAPE, "moe_import_reference_packed: the reference's groups are 128 along K (group=%d)", w->group);
+    if (!P || (w->bits != 16 && !Sc)) return fail(CKL_INVALID_ARG, "moe_import_reference_packed: P/Sc NULL");
+    if ((uintptr_t)P & 3) return fail(CKL_INVALID_ARG, "moe_import_reference_packed: P must be 4-byte aligned");
+    const cudaStream_t s = (cudaStream_t)stream;
+    if (w->bits != 16 && Sc != w->scales)    // the scales keep the reference's layout
+        CKL_CUDA_TRY(cudaMemcpyAsync(w->scales, Sc, ckl_moe_scale_count(w->E, w->K, w->N, w->group) * sizeof(__half),
+                                     cudaMemcpyDeviceToDevice, s));
+    const RefPackedSource src{P, w->K, w->N, w->bits};
+    pack_kernel<<<2048, 256, 0, s>>>(src, static_cast<const __half*>(w->bits != 16 ? w->scales : nullptr),
+                                     nullptr, static_cast<uint8_t*>(w->packed), w->E, w->K, w->N,
+                                     layout_group(w), w->bits, 0);
     CKL_CUDA_TRY(cudaGetLastError());
     return CKL_OK;
 }

@@ -98,7 +98,8 @@ CKL_API ckl_status ckl_decode_plan(int G, int B, int Hkv, int max_len, int force
                            int* num_chunks, int* chunk_tokens);
 
 /* Bytes of workspace ckl_decode_attention needs for these params (0 when the launch is a
- * single chunk and writes out/lse directly). */
+ * single chunk and writes out/lse directly; SIZE_MAX for shapes the launch rejects, e.g.
+ * part_stride > 65535). */
 CKL_API size_t ckl_decode_workspace_size(const ckl_decode_params* p);
 
 /* One launch of the partial kernel (decode_partial<G,V>, 01_decode_attention.cu:77-236):
@@ -147,7 +148,9 @@ CKL_API ckl_status ckl_decode_attention_balanced(const ckl_decode_params* p, voi
  *     32,500 partial rows B*Hq*num_chunks); larger launches return CKL_WORKSPACE_TOO_SMALL.
  *     chunk_base must be 0 and part_stride == num_chunks.
  *   - The first call on a device looks up the scratch's device address (and may load the
- *     library's device code); make that first call before any stream capture.
+ *     library's device code); make that first call before any stream capture. A failed
+ *     lookup is retried by the next call. The address kept is the primary context's: it
+ *     does not survive cudaDeviceReset.
  *   - All calls on a device share the one scratch and it keeps the last call's contents
  *     (each call rewrites every slot it reads). Calls that overlap on the GPU -- two
  *     streams, or two host threads -- race on it: serialise them.
@@ -307,6 +310,19 @@ CKL_API size_t ckl_moe_zero_words(int E, int K, int N, int group);
  * s = fp16((max(w,0) - min(w,0)) / 15), z = clamp(rn(-min(w,0)/s), 0, 15),
  * q = clamp(rn(w/s) + z, 0, 15). */
 CKL_API ckl_status ckl_moe_pack_weights(const void* W, ckl_moe_weights* w, void* stream);
+
+/* Imports weights the reference has already packed (QuantWeights' P and Sc,
+ * 03_moe_wq_decode.cu:281-299, written by pack_weights<BITS> 03:49-87): P (device) holds
+ * uint32 words in widx order (03:43-45) -- word ((e*(K/4) + k/4)*(N/CPT) + cw)*4 + k%4 has
+ * columns cw*CPT .. cw*CPT+CPT-1 (CPT = 32/bits) at bit offsets bits*c, offset-binary codes
+ * (q + 8 int4, q + 128 int8) or two fp16 values at 16 bits; Sc (device) the fp16 scales
+ * [E][K/128][N]. *w is caller-allocated as for ckl_moe_pack_weights with asym = 0 and
+ * group 128 (bits 4 and 8): the codes are re-laid into the packed records on the device
+ * (nothing is re-quantised) and Sc is copied into w->scales (which may be Sc itself).
+ * The result is bit-identical to ckl_moe_pack_weights on the weights the reference
+ * quantised. Asynchronous on `stream`. */
+CKL_API ckl_status ckl_moe_import_reference_packed(const uint32_t* P, const void* Sc,
+                                                   ckl_moe_weights* w, void* stream);
 
 /* The dequantised weights the GEMM uses, fp32 [E][K][N]: (q - z) * s exactly
  * (host_weight, 03_moe_wq_decode.cu:336-348). */

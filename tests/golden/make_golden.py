@@ -1,9 +1,11 @@
 """Regenerates the golden fixtures in this directory from the reference itself.
 
-Run in a container that has the reference tree (default /root/reference) and the
-reference-compiled oracle libraries (make -C oracle):
+Run where the reference tree is present, after building the reference-compiled oracle
+libraries (make -C oracle REF=<reference tree>):
 
-    python tests/golden/make_golden.py [--ref /root/reference]
+    python tests/golden/make_golden.py --ref <reference tree>
+
+(--ref defaults to the environment variable CKL_REFERENCE.)
 
 Fixtures written (all small):
   moe_decode_counts.json  per-expert routed counts published by the reference
@@ -39,8 +41,11 @@ def digests(bt):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", default=os.environ.get("CKL_REFERENCE"),
+                    help="the reference tree (default: $CKL_REFERENCE)")
     args = ap.parse_args()
+    if not args.ref or not os.path.isdir(args.ref):
+        sys.exit("make_golden: pass --ref <reference tree> (or set CKL_REFERENCE)")
     if O.ref01() is None or O.ref03() is None:
         sys.exit("oracle/_ref libraries missing: run make -C oracle (needs the reference tree)")
 

@@ -84,6 +84,51 @@ def test_packing_matches_reference_pack_weights(ckl, oracle, dev, bits):
         assert np.array_equal(q.scales.cpu().numpy().view(np.uint16), Scn.view(np.uint16))
 
 
+@pytest.mark.skipif(not os.path.exists(REF03), reason="reference not compiled here")
+@pytest.mark.parametrize("bits", [4, 8, 16])
+def test_import_reference_packed_weights(ckl, oracle, dev, bits):
+    """Weights packed by the reference's own pack_weights<bits> (03_moe_wq_decode.cu:49-87),
+    imported through ckl_moe_import_reference_packed: the dequantised weights equal the
+    reference's host_weight (03:336-348) bit for bit, the packed records equal our own
+    packer's from the same fp16 weights, and the expert GEMM over the imported weights
+    matches the fp64 oracle on the reference's GEMM case (T=40 tokens, top-2, 8 experts,
+    one of them empty)."""
+    import ctypes as C
+    import torch
+    E, d, f = 8, 2048, 200
+    W = oracle.init_uniform((E, d, f), 5 + 2, 1.0 / np.sqrt(d))
+    dW = T_(W, dev)
+    cpt = 32 // bits
+    P = torch.empty(E * d * (f // cpt), dtype=torch.int32, device=dev)
+    ns = E * (d // 128) * f if bits < 16 else 1
+    Sc = torch.empty(ns, dtype=torch.float16, device=dev)
+    L = oracle.ref03()
+    assert L.ref03_pack_weights_device(bits, C.c_void_p(dW.data_ptr()), C.c_void_p(P.data_ptr()),
+                                       C.c_void_p(Sc.data_ptr()), E, d, f) == 0
+    Pn = P.cpu().numpy().view(np.uint32)
+    Scn = Sc.cpu().numpy()
+    ref_w = np.empty((E, d, f), np.float32)
+    L.ref03_host_weight_all(bits, oracle._p(Pn), Pn.size, oracle._p(Scn), Scn.size, E, d, f,
+                            oracle._p(ref_w))
+    imp = ckl.QuantWeights.from_reference_packed(bits, P, Sc, E, d, f)
+    torch.cuda.synchronize()
+    got = imp.dequant().cpu().numpy()
+    assert np.array_equal(got.view(np.uint32), ref_w.view(np.uint32))
+    own = ckl.QuantWeights(bits, dW, group=128)
+    assert torch.equal(imp.packed, own.packed)
+    # expert GEMM over the imported weights: the reference's correctness case shape
+    T, k = 40, 2
+    lg = oracle.make_logits(T, E, 5, 3)                 # expert 3 receives no tokens
+    X = oracle.init_uniform((T, d), 5 + 1, 1.0)
+    r = ckl.route_and_permute(T_(lg, dev), T_(X, dev), k)
+    A = T * k
+    Yp = torch.empty((A, f), dtype=torch.float16, device=dev)
+    imp.run(r["Xp"], Yp, r["offsets"], A)
+    torch.cuda.synchronize()
+    ref = oracle.expert_gemm(r["Xp"].cpu().numpy(), ref_w, r["offsets"].cpu().numpy())
+    assert rel_rms(Yp.float().cpu().numpy(), ref) <= REL_RMS
+
+
 ROUTE_CASES = [(40, 8, 2, 3, 5), (64, 64, 6, -1, 9), (1, 64, 6, -1, 9), (16, 8, 2, -1, 9),
                (100, 8, 2, -1, 5), (37, 16, 4, 3, 5), (300, 256, 8, -1, 1)]
 
@@ -209,6 +254,84 @@ def _layer_weights(ckl, oracle, dev, E, d, F, mode, seed=11):
         g = kw.get("group") or W.shape[1]
         return ckl.QuantWeights(kw["bits"], T_(W, dev), group=g, asym=kw.get("asym", False))
     return q(Wg), q(Wu), q(Wd)
+
+
+@pytest.mark.parametrize("mode", ["int4", "int8pc", "fp16", "int4sym"])
+@pytest.mark.parametrize("T", [1, 5, 33])
+def test_moe_layer_against_fp64_oracle(ckl, oracle, dev, mode, T):
+    import torch
+    E, k, d, F = 8, 2, 256, 384
+    gq, uq, dq = _layer_weights(ckl, oracle, dev, E, d, F, mode)
+    lg = oracle.normal((T, E), seed=100 + T, fp16=False)
+    X = oracle.normal((T, d), seed=200 + T)
+    layer = ckl.MoeLayer(gq, uq, dq)
+    ids = torch.empty((T, k), dtype=torch.int32, device=dev)
+    wts = torch.empty((T, k), dtype=torch.float32, device=dev)
+    out = layer.forward(T_(lg, dev), T_(X, dev), k, ids=ids, wts=wts)
+    torch.cuda.synchronize()
+    ckl.check_device_error()
+    rids, rwts = oracle.route(lg, k)
+    assert np.array_equal(ids.cpu().numpy(), rids)
+    ref = oracle.moe_layer(X, rids, rwts, gq.dequant().cpu().numpy(), uq.dequant().cpu().numpy(),
+                           dq.dequant().cpu().numpy())
+    assert rel_rms(out.float().cpu().numpy(), ref) <= REL_RMS
+    again = layer.forward(T_(lg, dev), T_(X, dev), k)
+    assert torch.equal(out, again)                     # deterministic
+
+
+@pytest.mark.parametrize("T", [1, 4, 16, 64])
+def test_config4_w4a16_layer_full_size(ckl, oracle, dev, T):
+    """E=64, top-6, d=2048, F=1408, asymmetric int4 g128, weights
+    N(0,0.02), activations and logits N(0,1). Routing ids bit-exact for the whole batch;
+    the output of up to 8 sampled tokens against the fp64 oracle (rel-RMS <= 1e-2)."""
+    import torch
+    from moe_ref import rel_rms as rr, sample_tokens, sampled_layer_ref
+    E, k, d, F = 64, 6, 2048, 1408
+    g = torch.Generator(device=dev)
+    g.manual_seed(4)
+    mk = lambda *s: (torch.randn(*s, generator=g, device=dev) * 0.02).half()
+    gq = ckl.QuantWeights(4, mk(E, d, F), group=128, asym=True)
+    uq = ckl.QuantWeights(4, mk(E, d, F), group=128, asym=True)
+    dq = ckl.QuantWeights(4, mk(E, F, d), group=128, asym=True)
+    lg = torch.randn((T, E), generator=g, device=dev)
+    X = torch.randn((T, d), generator=g, device=dev).half()
+    ids = torch.empty((T, k), dtype=torch.int32, device=dev)
+    wts = torch.empty((T, k), dtype=torch.float32, device=dev)
+    out = ckl.MoeLayer(gq, uq, dq).forward(lg, X, k, ids=ids, wts=wts)
+    torch.cuda.synchronize()
+    ckl.check_device_error()
+    tok = sample_tokens(T)
+    ref, rids = sampled_layer_ref(oracle, lg.cpu().numpy(), X.cpu().numpy(), k, gq, uq, dq, tok)
+    assert np.array_equal(ids.cpu().numpy(), rids)
+    assert rr(out.float().cpu().numpy()[tok], ref) <= REL_RMS
+
+
+def test_config5_w8a16_moe_full_size(ckl, oracle, dev):
+    """BASELINE config 5 MoE block: E=8, top-2, d=4096, F=14336, int8 per output channel,
+    weights N(0,0.02), T=32. Routing ids bit-exact; 8 sampled tokens against the fp64
+    oracle (rel-RMS <= 1e-2)."""
+    import torch
+    from moe_ref import rel_rms as rr, sample_tokens, sampled_layer_ref
+    E, k, d, F, T = 8, 2, 4096, 14336, 32
+    g = torch.Generator(device=dev)
+    g.manual_seed(5)
+    mk = lambda *s: (torch.randn(*s, generator=g, device=dev) * 0.02).half()
+    gq = ckl.QuantWeights(8, mk(E, d, F), group=d)
+    uq = ckl.QuantWeights(8, mk(E, d, F), group=d)
+    dq = ckl.QuantWeights(8, mk(E, F, d), group=F)
+    lg = torch.randn((T, E), generator=g, device=dev)
+    X = torch.randn((T, d), generator=g, device=dev).half()
+    ids = torch.empty((T, k), dtype=torch.int32, device=dev)
+    wts = torch.empty((T, k), dtype=torch.float32, device=dev)
+    out = ckl.MoeLayer(gq, uq, dq).forward(lg, X, k, ids=ids, wts=wts)
+    torch.cuda.synchronize()
+    ckl.check_device_error()
+    tok = sample_tokens(T)
+    ref, rids = sampled_layer_ref(oracle, lg.cpu().numpy(), X.cpu().numpy(), k, gq, uq, dq, tok)
+    assert np.array_equal(ids.cpu().numpy(), rids)
+    assert rr(out.float().cpu().numpy()[tok], ref) <= REL_RMS
+    del gq, uq, dq
+    torch.cuda.empty_cache()
 
 
 @pytest.mark.parametrize("mode", ["int4", "int8pc", "fp16", "int4sym"])
