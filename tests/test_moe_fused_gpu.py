@@ -1,0 +1,149 @@
+"""GPU parity of the fused W4A16 MoE layer kernel (one persistent kernel for gate/up + down,
+csrc/moe_fused.cu), which ckl_moe_layer runs for int4 group-128 weights with d, F <= 2048.
+
+Each case is checked against the fp64 oracle (rel-RMS <= 1e-2) and
+against the unfused path -- the same layer assembled from the single-GEMM entry points
+(ckl_moe_route_permute, ckl_moe_expert_gemm_ex with SwiGLU, ckl_moe_expert_gemm_ex,
+ckl_moe_combine), which differ from the fused kernel only in the fp32 summation order of K
+(rel-RMS <= 1e-3 between the two). Cases: experts with more than 16 rows (several passes),
+grids with more CTAs than 128-k groups (empty CTA ranges), 256 experts, symmetric codes,
+CUDA-graph replay, run-to-run bit identity.
+"""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+REL_RMS = 1e-2
+
+
+def T_(a, dev):
+    import torch
+    return torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+
+
+def _weights(ckl, oracle, dev, E, d, F, asym=True, seed=11, std=0.02):
+    Ws = [oracle.normal((E, d, F), seed=seed, std=std), oracle.normal((E, d, F), seed=seed + 1, std=std),
+          oracle.normal((E, F, d), seed=seed + 2, std=std)]
+    return [ckl.QuantWeights(4, T_(W, dev), group=128, asym=asym) for W in Ws]
+
+
+def _unfused(ckl, lg, X, k, gq, uq, dq):
+    """The layer from the single-GEMM entry points (moe_gemm.cu's kernel)."""
+    T = X.shape[0]
+    r = ckl.route_and_permute(lg, X, k)
+    A = T * k
+    h = ckl.expert_gemm_ex(r["Xp"], None, r["offsets"], A, gq, uq)
+    y = ckl.expert_gemm_ex(h, None, r["offsets"], A, dq, None, y_f32=True)
+    return ckl.combine(y, r["inv_perm"], r["wts"], T, k)
+
+
+def _check(ckl, oracle, dev, T, E, k, d, F, asym=True, seed=0):
+    import torch
+    from moe_ref import rel_rms
+    gq, uq, dq = _weights(ckl, oracle, dev, E, d, F, asym=asym, seed=11 + seed)
+    lg = oracle.normal((T, E), seed=100 + T + seed, fp16=False)
+    X = oracle.normal((T, d), seed=200 + T + seed)
+    layer = ckl.MoeLayer(gq, uq, dq)
+    ids = torch.empty((T, k), dtype=torch.int32, device=dev)
+    out = layer.forward(T_(lg, dev), T_(X, dev), k, ids=ids)
+    torch.cuda.synchronize()
+    ckl.check_device_error()
+    rids, rwts = oracle.route(lg, k)
+    assert np.array_equal(ids.cpu().numpy(), rids)
+    ref = oracle.moe_layer(X, rids, rwts, gq.dequant().cpu().numpy(), uq.dequant().cpu().numpy(),
+                           dq.dequant().cpu().numpy())
+    got = out.float().cpu().numpy()
+    assert np.isfinite(got).all()
+    assert rel_rms(got, ref) <= REL_RMS
+    base = _unfused(ckl, T_(lg, dev), T_(X, dev), k, gq, uq, dq)
+    torch.cuda.synchronize()
+    assert rel_rms(got, base.float().cpu().numpy()) <= 1e-3
+    again = layer.forward(T_(lg, dev), T_(X, dev), k)
+    torch.cuda.synchronize()
+    assert torch.equal(out, again)                     # bit-identical repeat
+    return counts_of(rids, E)
+
+
+def counts_of(ids, E):
+    return np.bincount(np.asarray(ids).ravel(), minlength=E)
+
+
+@pytest.mark.parametrize("T", [1, 2, 7, 33])
+def test_fused_small_layer_empty_cta_ranges(ckl, oracle, dev, T):
+    """E=8, top-2, d=256, F=384: at most a few hundred 128-k groups, fewer than CTAs for small
+    T (some CTAs own no work, units cut between many CTAs)."""
+    _check(ckl, oracle, dev, T, 8, 2, 256, 384)
+
+
+@pytest.mark.parametrize("T", [100, 300])
+def test_fused_experts_over_16_rows(ckl, oracle, dev, T):
+    """Experts with 25-75 rows: two to five passes of 16 rows over the same weights."""
+    cnt = _check(ckl, oracle, dev, T, 8, 2, 512, 640)
+    assert cnt.max() > 32
+
+
+def test_fused_symmetric_codes(ckl, oracle, dev):
+    _check(ckl, oracle, dev, 24, 16, 4, 512, 256, asym=False)
+
+
+def test_fused_256_experts(ckl, oracle, dev):
+    _check(ckl, oracle, dev, 64, 256, 8, 256, 512)
+
+
+@pytest.mark.parametrize("T", [1, 16])
+def test_fused_config4_against_unfused(ckl, oracle, dev, T):
+    """BASELINE config 4 (E=64, top-6, d=2048, F=1408) at full size: the fused layer against
+    the unfused path over all tokens (the fp64 check on sampled tokens is in
+    test_moe_gpu.py)."""
+    import torch
+    from moe_ref import rel_rms
+    E, k, d, F = 64, 6, 2048, 1408
+    g = torch.Generator(device=dev)
+    g.manual_seed(40 + T)
+    mk = lambda *s: (torch.randn(*s, generator=g, device=dev) * 0.02).half()
+    gq, uq = (ckl.QuantWeights(4, mk(E, d, F), group=128, asym=True) for _ in range(2))
+    dq = ckl.QuantWeights(4, mk(E, F, d), group=128, asym=True)
+    lg = torch.randn((T, E), generator=g, device=dev)
+    X = torch.randn((T, d), generator=g, device=dev).half()
+    out = ckl.MoeLayer(gq, uq, dq).forward(lg, X, k)
+    base = _unfused(ckl, lg, X, k, gq, uq, dq)
+    torch.cuda.synchronize()
+    ckl.check_device_error()
+    assert rel_rms(out.float().cpu().numpy(), base.float().cpu().numpy()) <= 1e-3
+
+
+def test_fused_layer_in_cuda_graph(ckl, oracle, dev):
+    """Captured once, replayed with new inputs copied into the same buffers: each replay
+    equals the eager call on those inputs."""
+    import torch
+    E, k, d, F, T = 64, 6, 2048, 1408, 4
+    g = torch.Generator(device=dev)
+    g.manual_seed(77)
+    mk = lambda *s: (torch.randn(*s, generator=g, device=dev) * 0.02).half()
+    gq, uq = (ckl.QuantWeights(4, mk(E, d, F), group=128, asym=True) for _ in range(2))
+    dq = ckl.QuantWeights(4, mk(E, F, d), group=128, asym=True)
+    layer = ckl.MoeLayer(gq, uq, dq)
+    lg = torch.randn((T, E), generator=g, device=dev)
+    X = torch.randn((T, d), generator=g, device=dev).half()
+    out = torch.empty((T, d), dtype=torch.float16, device=dev)
+    ws = torch.empty(layer.workspace_size(T, k), dtype=torch.uint8, device=dev)
+    s = torch.cuda.Stream(device=dev)
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        layer.forward(lg, X, k, out=out, workspace=ws)
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        layer.forward(lg, X, k, out=out, workspace=ws)
+    for it in range(3):
+        lg.copy_(torch.randn((T, E), generator=g, device=dev))
+        X.copy_(torch.randn((T, d), generator=g, device=dev).half())
+        graph.replay()
+        torch.cuda.synchronize()
+        eager = layer.forward(lg, X, k)
+        torch.cuda.synchronize()
+        assert torch.equal(out, eager), f"replay {it}"
+    ckl.check_device_error()
+    del graph
