@@ -60,6 +60,9 @@ def parse():
                     help="skip the extra rows (sweep, cascades, MoE, Mixtral, grouped GEMM)")
     ap.add_argument("--extras", default="",
                     help="comma-separated names of the extra rows to run (default: all)")
+    ap.add_argument("--probe", default="",
+                    help="run one small fixed workload a few times (L2 flushed between calls) "
+                         "for a profiler and exit: " + ", ".join(sorted(PROBES)))
     return ap.parse_args()
 
 
@@ -1234,8 +1237,128 @@ def run_ours(args):
     return 0
 
 
+# ------------------------------------------------------------------ profiler probes
+# Each probe builds one workload of the bench rows above, calls it `calls` times with a 512 MB
+# memset between calls (cold L2, as in the timed rows) and prints the CUDA-event median. They
+# are the commands behind the ncu summaries in profiles/ (run them under ncu with -k / -s / -c
+# to pick the launches), small enough for a multi-pass capture: a few hundred MB on the device.
+def _probe_moe_layer(ckl, dev, T, calls):
+    import torch
+    E, k, d, F = 64, 6, 2048, 1408
+    g = torch.Generator(device=dev)
+    g.manual_seed(44)
+    mk = lambda *sh: (torch.randn(*sh, generator=g, device=dev) * 0.02).half()
+    q = [ckl.QuantWeights(4, mk(E, d, F), group=128, asym=True) for _ in range(2)]
+    q.append(ckl.QuantWeights(4, mk(E, F, d), group=128, asym=True))
+    layer = ckl.MoeLayer(*q)
+    lg = torch.randn((T, E), generator=g, device=dev)
+    X = torch.randn((T, d), generator=g, device=dev).half()
+    out = torch.empty((T, d), dtype=torch.float16, device=dev)
+    ws = torch.empty(layer.workspace_size(T, k), dtype=torch.uint8, device=dev)
+    return lambda: layer.forward(lg, X, k, out=out, workspace=ws)
+
+
+def _probe_moe_unfused(ckl, dev, T, calls):
+    """The layer's two expert GEMMs through the single-GEMM entry point (moe_gemm.cu)."""
+    import torch
+    E, k, d, F = 64, 6, 2048, 1408
+    g = torch.Generator(device=dev)
+    g.manual_seed(44)
+    mk = lambda *sh: (torch.randn(*sh, generator=g, device=dev) * 0.02).half()
+    gq, uq = (ckl.QuantWeights(4, mk(E, d, F), group=128, asym=True) for _ in range(2))
+    dq = ckl.QuantWeights(4, mk(E, F, d), group=128, asym=True)
+    lg = torch.randn((T, E), generator=g, device=dev)
+    X = torch.randn((T, d), generator=g, device=dev).half()
+    r = ckl.route_and_permute(lg, X, k)
+    A = T * k
+
+    def run():
+        h = ckl.expert_gemm_ex(r["Xp"], None, r["offsets"], A, gq, uq)
+        ckl.expert_gemm_ex(h, None, r["offsets"], A, dq, None, y_f32=True)
+    return run
+
+
+def _probe_cascade_tree(ckl, dev, calls):
+    import numpy as np
+    import torch
+    d, (lens, indptr, indices), _ = tree_batch(1024, 4096, 4, np.full(64, 256), dev, seed=23)
+    base = ckl.make_params(**d, num_chunks=1, chunk_tokens=16)
+    tp = ckl.plan_cascade_tree(base, indptr, indices, lens, 256)
+    ws = torch.empty(max(ckl.cascade_tree_workspace_size(tp), 256), dtype=torch.uint8, device=dev)
+    out = torch.empty_like(d["q"])
+    lse = torch.empty((len(lens), HQ), dtype=torch.float32, device=dev)
+    return lambda: ckl.cascade_tree_decode(tp, out=out, lse=lse, workspace=ws)
+
+
+def _probe_cascade_config3(ckl, dev, calls):
+    import numpy as np
+    import torch
+    lens = (4096 + np.full(64, 256)).astype(np.int32)
+    d, (lens, indptr, indices) = paged_batch(lens, dev, seed=21, Lp=4096)
+    base = ckl.make_params(**d, num_chunks=1, chunk_tokens=16)
+    cp = ckl.plan_cascade(base, indptr, indices, lens, 256)
+    ws = torch.empty(max(ckl.cascade_workspace_size(cp), 256), dtype=torch.uint8, device=dev)
+    out = torch.empty_like(d["q"])
+    lse = torch.empty((len(lens), HQ), dtype=torch.float32, device=dev)
+    return lambda: ckl.cascade_decode(cp, out=out, lse=lse, workspace=ws)
+
+
+def _probe_grouped(ckl, dev, calls):
+    import torch
+    T, E, k, d, f = 512, 8, 2, 4096, 14336
+    g = torch.Generator(device=dev)
+    g.manual_seed(T + E)
+    lg = torch.randn((T, E), generator=g, device=dev)
+    X = (torch.rand((T, d), generator=g, device=dev) * 2 - 1).half()
+    W = ((torch.rand((E, d, f), generator=g, device=dev) * 2 - 1) / d ** 0.5).half()
+    r = ckl.route_and_permute(lg, X, k)
+    out = torch.empty((T * k, f), dtype=torch.float16, device=dev)
+    return lambda: ckl.grouped_gemm(r["Xp"], W, r["offsets"], out=out)
+
+
+def _probe_decode(ckl, dev, name, calls):
+    import torch
+    lens = lengths(name)
+    d, _ = paged_batch(lens, dev, seed=7)
+    nc, ct = ckl.plan_chunks(HQ // HKV, len(lens), HKV, int(lens.max()))
+    p = ckl.make_params(**d, num_chunks=nc, chunk_tokens=ct)
+    out = torch.empty_like(d["q"])
+    lse = torch.empty((len(lens), HQ), dtype=torch.float32, device=dev)
+    ws = torch.empty(max(ckl.workspace_size(p), 256), dtype=torch.uint8, device=dev)
+    return lambda: ckl.decode_attention(**d, num_chunks=nc, chunk_tokens=ct, out=out, lse=lse,
+                                        workspace=ws)
+
+
+PROBES = {
+    **{f"moe_layer_T{T}": (lambda T: lambda ckl, dev, c: _probe_moe_layer(ckl, dev, T, c))(T)
+       for T in (1, 4, 16, 64)},
+    **{f"moe_unfused_T{T}": (lambda T: lambda ckl, dev, c: _probe_moe_unfused(ckl, dev, T, c))(T)
+       for T in (1, 64)},
+    "cascade_tree": _probe_cascade_tree,
+    "cascade_config3": _probe_cascade_config3,
+    "grouped_mixtral_T512": _probe_grouped,
+    "decode_64x1024": lambda ckl, dev, c: _probe_decode(ckl, dev, "64x1024", c),
+    "decode_1x32768": lambda ckl, dev, c: _probe_decode(ckl, dev, "1x32768", c),
+}
+
+
+def run_probe(args, calls=6):
+    import torch
+    import ckl
+    dev = torch.device("cuda", 0)
+    fn = PROBES[args.probe](ckl, dev, calls)
+    timer = ColdTimer(dev)
+    ms = timer(fn, iters=calls, warmup=3)
+    torch.cuda.synchronize()
+    ckl.check_device_error()
+    print(json.dumps({"probe": args.probe, "calls": calls + 3, "median_ms_cold": ms}))
+    return 0
+
+
 def main():
     args = parse()
+    if args.probe:
+        return run_probe(args)
     if args.impl == "reference":
         return run_reference(args)
     return run_ours(args)

@@ -354,6 +354,23 @@ def ref01():
         L.ref01_sample_run.argtypes = [vp, C.POINTER(C.c_double)]
         L.ref01_sample_free.restype = None
         L.ref01_sample_free.argtypes = [vp]
+        # the reference's GPU path (same-box comparator; needs a GPU)
+        L.ref01_decode_plan.restype = vp
+        L.ref01_decode_plan.argtypes = [vp, vp, vp, vp, vp, vp, i, i, i, i, i]
+        L.ref01_decode_plan_chunks.restype = i
+        L.ref01_decode_plan_chunks.argtypes = [vp]
+        L.ref01_decode_run.restype = None
+        L.ref01_decode_run.argtypes = [vp, vp, vp, vp]
+        L.ref01_decode_free.restype = None
+        L.ref01_decode_free.argtypes = [vp]
+        L.ref01_cascade_plan.restype = vp
+        L.ref01_cascade_plan.argtypes = [vp, vp, vp, vp, vp, vp, vp, vp, vp, i, i, i, i]
+        L.ref01_cascade_use.restype = i
+        L.ref01_cascade_use.argtypes = [vp]
+        L.ref01_cascade_run.restype = None
+        L.ref01_cascade_run.argtypes = [vp, vp, vp, vp]
+        L.ref01_cascade_free.restype = None
+        L.ref01_cascade_free.argtypes = [vp]
         _ref01 = L
     return _ref01
 
@@ -375,6 +392,12 @@ def ref03():
         L.ref03_pack_weights_device.argtypes = [i, vp, vp, vp, i, i, i]
         L.ref03_router_topk_device.restype = i
         L.ref03_router_topk_device.argtypes = [vp, vp, vp, i, i, i]
+        L.ref03_quant_make.restype = vp
+        L.ref03_quant_make.argtypes = [i, vp, i, i, i]
+        L.ref03_quant_run.restype = None
+        L.ref03_quant_run.argtypes = [vp, vp, vp, vp, i, i, i, i, i, vp]
+        L.ref03_quant_free.restype = None
+        L.ref03_quant_free.argtypes = [vp]
         _ref03 = L
     return _ref03
 

@@ -5,8 +5,9 @@
 // common/moe.cuh), from where it lies in the reference tree, into oracle/_ref/libref03.so.
 // Exposes make_logits (common/moe.cuh:142-151), host_weight (03_moe_wq_decode.cu:336-348),
 // and -- for GPU-side pinning on a box with a GPU -- the reference's pack_weights kernel
-// (03_moe_wq_decode.cu:49-87) and router_topk kernel (common/moe.cuh:23-72). No reference
-// code is copied into this repository.
+// (03_moe_wq_decode.cu:49-87), router_topk kernel (common/moe.cuh:23-72) and QuantWeights
+// (03:281-333) for the same-box GPU comparison. No reference code is copied into this
+// repository.
 
 #include <cstdint>
 #include <cstring>
@@ -51,5 +52,21 @@ int ref03_router_topk_device(const float* logits, int* ids, float* wts, int T, i
     cudaError_t e = cudaDeviceSynchronize();
     return e == cudaSuccess ? 0 : (int)e;
 }
+
+// The reference's QuantWeights (03:281-333) on a caller device W (packs with its own
+// pack_weights<bits>), and QuantWeights::run on caller device Xp / Yp / offsets (needs a GPU).
+void* ref03_quant_make(int bits, const void* W, int E, int d, int f) {
+    QuantWeights* q = new QuantWeights(bits, (const half*)W, E, d, f);
+    cudaDeviceSynchronize();
+    return q;
+}
+
+void ref03_quant_run(void* qw, const void* Xp, void* Yp, const int* offsets, int A, int E, int d,
+                     int f, int force_ksplit, void* stream) {
+    static_cast<QuantWeights*>(qw)->run((const half*)Xp, (half*)Yp, offsets, A, E, d, f,
+                                        force_ksplit, (cudaStream_t)stream);
+}
+
+void ref03_quant_free(void* qw) { delete static_cast<QuantWeights*>(qw); }
 
 }  // extern "C"
