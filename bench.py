@@ -1258,7 +1258,7 @@ def _probe_moe_layer(ckl, dev, T, calls):
     return lambda: layer.forward(lg, X, k, out=out, workspace=ws)
 
 
-def _probe_moe_unfused(ckl, dev, T, calls):
+def _probe_moe_gemms(ckl, dev, T, calls):
     """The layer's two expert GEMMs through the single-GEMM entry point (moe_gemm.cu)."""
     import torch
     E, k, d, F = 64, 6, 2048, 1408
@@ -1332,7 +1332,7 @@ def _probe_decode(ckl, dev, name, calls):
 PROBES = {
     **{f"moe_layer_T{T}": (lambda T: lambda ckl, dev, c: _probe_moe_layer(ckl, dev, T, c))(T)
        for T in (1, 4, 16, 64)},
-    **{f"moe_unfused_T{T}": (lambda T: lambda ckl, dev, c: _probe_moe_unfused(ckl, dev, T, c))(T)
+    **{f"moe_gemms_T{T}": (lambda T: lambda ckl, dev, c: _probe_moe_gemms(ckl, dev, T, c))(T)
        for T in (1, 64)},
     "cascade_tree": _probe_cascade_tree,
     "cascade_config3": _probe_cascade_config3,

@@ -2,8 +2,6 @@
 // moe_ep.cu); one declaration, so that the three agree on every signature.
 #pragma once
 
-#include <cuda_fp16.h>
-
 #include "ckl_internal.h"
 
 namespace ckl {
@@ -23,22 +21,6 @@ ckl_status expert_gemm(const void* X, const int* row_src, const int* offsets, in
 // expert-sorted row).
 ckl_status route_tokens(const float* logits, int T, int E, int k, int* ids, float* wts,
                         int* counts, int* offsets, int* inv_perm, int* row_src, cudaStream_t s);
-
-// The fused gate/up + down persistent kernel (moe_fused.cu): whether the layer's weights
-// qualify (int4 group 128, d and F <= 2048, multiples of 64), the extra workspace it needs
-// (partials of units cut between CTAs, then counters the routing kernel zeroes), and its
-// launch (programmatic dependent launch on the routing kernel).
-bool fused_eligible(const ckl_moe_weights* gate, const ckl_moe_weights* up,
-                    const ckl_moe_weights* down);
-struct FusedWs {
-    size_t part, cnt, total;
-    int cnt_words, up0_max, up1_max;
-};
-FusedWs fused_ws(int T, int k, int E, int d, int F, int sms);
-ckl_status launch_fused(const void* X, const int* offsets, const int* row_src, int T, int k,
-                        const ckl_moe_weights* gate, const ckl_moe_weights* up,
-                        const ckl_moe_weights* down, __half* h, float* y, void* fws,
-                        cudaStream_t s);
 
 }  // namespace moe
 }  // namespace ckl

@@ -45,8 +45,7 @@ constexpr int ROUTE_SMEM_LOGITS = 6144;   // logits staged in shared memory (24 
 __global__ void __launch_bounds__(ROUTE_THREADS)
 route_kernel(const float* __restrict__ logits, int T, int E, int k, int* __restrict__ ids,
              float* __restrict__ wts, int* __restrict__ counts, int* __restrict__ offsets,
-             int* __restrict__ inv_perm, int* __restrict__ row_src, int bm, int* __restrict__ tiles,
-             int* __restrict__ zero, int zero_n) {
+             int* __restrict__ inv_perm, int* __restrict__ row_src, int bm, int* __restrict__ tiles) {
     __shared__ __align__(16) int s_ids[MAX_A];
     __shared__ int s_cnt[MAX_E];
     __shared__ int s_off[MAX_E + 1];
@@ -55,8 +54,6 @@ route_kernel(const float* __restrict__ logits, int T, int E, int k, int* __restr
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int A = T * k;
     pdl_trigger();                    // the expert GEMM may launch; it waits for our results
-    for (int i = threadIdx.x; i < zero_n; i += blockDim.x) zero[i] = 0;   // counters of the
-                                                                          // fused expert kernel
     for (int e = threadIdx.x; e < E; e += blockDim.x) s_cnt[e] = 0;
     const bool staged = T * (E + 1) <= ROUTE_SMEM_LOGITS;    // the launch sized s_lg for this
     const int lg_stride = E + 1;
@@ -243,8 +240,7 @@ ckl_status route_tokens(const float* logits, int T, int E, int k, int* ids, floa
     ckl_status st = route_setup();
     if (st != CKL_OK) return st;
     route_kernel<<<1, ROUTE_THREADS, route_smem(T, E), s>>>(logits, T, E, k, ids, wts, counts,
-                                                            offsets, inv_perm, row_src, 1, nullptr,
-                                                            nullptr, 0);
+                                                            offsets, inv_perm, row_src, 1, nullptr);
     CKL_CUDA_TRY(cudaGetLastError());
     return CKL_OK;
 }
@@ -303,8 +299,7 @@ ckl_status ckl_moe_route_permute(const float* logits, const void* X, int T, int 
     st = route_setup();
     if (st != CKL_OK) return st;
     route_kernel<<<1, ROUTE_THREADS, route_smem(T, E), s>>>(logits, T, E, k, ids, wts, counts,
-                                                            offsets, inv_perm, nullptr, bm, tiles,
-                                                            nullptr, 0);
+                                                            offsets, inv_perm, nullptr, bm, tiles);
     CKL_CUDA_TRY(cudaGetLastError());
     if (Xp) {
         permute_rows_kernel<<<T * k, 128, 0, s>>>(static_cast<const __half*>(X), inv_perm,
@@ -335,13 +330,7 @@ size_t ckl_moe_layer_workspace_size(int T, int k, const ckl_moe_weights* gate,
     const int A = T * k;
     const size_t s1 = ckl_moe_gemm_workspace_size(gate, A, 1, 0);
     const size_t s2 = ckl_moe_gemm_workspace_size(down, A, 0, 0);
-    size_t total = layer_ws(T, gate->E, k, down->N, gate->N, std::max(s1, s2)).total;
-    if (fused_eligible(gate, gate, down)) {
-        const DeviceInfo* di = device_info();
-        if (!di) return 0;
-        total += fused_ws(T, k, gate->E, gate->K, gate->N, di->sms).total;
-    }
-    return total;
+    return layer_ws(T, gate->E, k, down->N, gate->N, std::max(s1, s2)).total;
 }
 
 ckl_status ckl_moe_layer(const float* logits, const void* X, int T, int k,
@@ -360,13 +349,8 @@ ckl_status ckl_moe_layer(const float* logits, const void* X, int T, int k,
     const size_t s1 = ckl_moe_gemm_workspace_size(gate, A, 1, 0);
     const size_t s2 = ckl_moe_gemm_workspace_size(down, A, 0, 0);
     const LayerWs L = layer_ws(T, E, k, d, F, std::max(s1, s2));
-    const bool fused = fused_eligible(gate, up, down) && ((uintptr_t)X & 15) == 0;
-    const DeviceInfo* di = device_info();
-    if (!di) return CKL_CUDA_ERROR;
-    const FusedWs FW = fused ? fused_ws(T, k, E, d, F, di->sms) : FusedWs{};
-    const size_t need = L.total + FW.total;
-    if (!workspace || workspace_bytes < need)
-        return fail(CKL_WORKSPACE_TOO_SMALL, "moe_layer needs %zu workspace bytes, got %zu", need,
+    if (!workspace || workspace_bytes < L.total)
+        return fail(CKL_WORKSPACE_TOO_SMALL, "moe_layer needs %zu workspace bytes, got %zu", L.total,
                     workspace_bytes);
     if ((uintptr_t)workspace & 255) return fail(CKL_INVALID_ARG, "workspace must be 256-byte aligned");
     uint8_t* ws = static_cast<uint8_t*>(workspace);
@@ -384,24 +368,8 @@ ckl_status ckl_moe_layer(const float* logits, const void* X, int T, int k,
 
     st = route_setup();
     if (st != CKL_OK) return st;
-    if (fused) {
-        // route (and zero the fused kernel's counters) -> gate/up + down in one persistent
-        // kernel -> combine; the last two wait for their predecessor through PDL
-        uint8_t* fws = ws + L.total;
-        route_kernel<<<1, ROUTE_THREADS, route_smem(T, E), s>>>(
-            logits, T, E, k, ids, wts, counts, offsets, inv_perm, row_src, 1, nullptr,
-            reinterpret_cast<int*>(fws + FW.cnt), FW.cnt_words);
-        CKL_CUDA_TRY(cudaGetLastError());
-        st = launch_fused(X, offsets, row_src, T, k, gate, up, down, h, y, fws, s);
-        if (st != CKL_OK) return st;
-        void* cargs[] = {&y, &inv_perm, &wts, &out, &k, const_cast<int*>(&d)};
-        CKL_CUDA_TRY(launch(reinterpret_cast<const void*>(combine_kernel<true>), dim3(T), dim3(256),
-                            0, s, cargs, true));
-        return CKL_OK;
-    }
     route_kernel<<<1, ROUTE_THREADS, route_smem(T, E), s>>>(logits, T, E, k, ids, wts, counts,
-                                                            offsets, inv_perm, row_src, 1, nullptr,
-                                                            nullptr, 0);
+                                                            offsets, inv_perm, row_src, 1, nullptr);
     CKL_CUDA_TRY(cudaGetLastError());
     // gate/up waits for the routing; down prefetches its first weight stages while gate/up
     // finishes (its offsets are the routing's, one kernel older); combine waits for down.

@@ -1,13 +1,11 @@
-"""GPU parity of the fused W4A16 MoE layer kernel (one persistent kernel for gate/up + down,
-csrc/moe_fused.cu), which ckl_moe_layer runs for int4 group-128 weights with d, F <= 2048.
+"""GPU parity of the W4A16 SwiGLU MoE layer (ckl_moe_layer) on shapes beyond the reference's.
 
-Each case is checked against the fp64 oracle (rel-RMS <= 1e-2) and
-against the unfused path -- the same layer assembled from the single-GEMM entry points
-(ckl_moe_route_permute, ckl_moe_expert_gemm_ex with SwiGLU, ckl_moe_expert_gemm_ex,
-ckl_moe_combine), which differ from the fused kernel only in the fp32 summation order of K
-(rel-RMS <= 1e-3 between the two). Cases: experts with more than 16 rows (several passes),
-grids with more CTAs than 128-k groups (empty CTA ranges), 256 experts, symmetric codes,
-CUDA-graph replay, run-to-run bit identity.
+Each case is checked against the fp64 oracle (rel-RMS <= 1e-2), against
+the same layer assembled from the single-GEMM entry points (ckl_moe_route_permute,
+ckl_moe_expert_gemm_ex with SwiGLU, ckl_moe_expert_gemm_ex, ckl_moe_combine; rel-RMS <= 1e-3),
+with routing ids bit-exact against the oracle and run-to-run bit identity. Cases: grids
+with more CTAs than work, experts with more than 16 rows (several passes), 256 experts,
+symmetric codes, a larger batch, config 4 at full size, CUDA-graph replay.
 """
 import numpy as np
 import pytest
@@ -29,7 +27,7 @@ def _weights(ckl, oracle, dev, E, d, F, asym=True, seed=11, std=0.02):
 
 
 def _unfused(ckl, lg, X, k, gq, uq, dq):
-    """The layer from the single-GEMM entry points (moe_gemm.cu's kernel)."""
+    """The layer from the single-GEMM entry points."""
     T = X.shape[0]
     r = ckl.route_and_permute(lg, X, k)
     A = T * k
@@ -70,31 +68,30 @@ def counts_of(ids, E):
 
 
 @pytest.mark.parametrize("T", [1, 2, 7, 33])
-def test_fused_small_layer_empty_cta_ranges(ckl, oracle, dev, T):
-    """E=8, top-2, d=256, F=384: at most a few hundred 128-k groups, fewer than CTAs for small
-    T (some CTAs own no work, units cut between many CTAs)."""
+def test_layer_small(ckl, oracle, dev, T):
+    """E=8, top-2, d=256, F=384: far fewer work items than CTAs for small T."""
     _check(ckl, oracle, dev, T, 8, 2, 256, 384)
 
 
 @pytest.mark.parametrize("T", [100, 300])
-def test_fused_experts_over_16_rows(ckl, oracle, dev, T):
+def test_layer_experts_over_16_rows(ckl, oracle, dev, T):
     """Experts with 25-75 rows: two to five passes of 16 rows over the same weights."""
     cnt = _check(ckl, oracle, dev, T, 8, 2, 512, 640)
     assert cnt.max() > 32
 
 
-def test_fused_symmetric_codes(ckl, oracle, dev):
+def test_layer_symmetric_codes(ckl, oracle, dev):
     _check(ckl, oracle, dev, 24, 16, 4, 512, 256, asym=False)
 
 
-def test_fused_256_experts(ckl, oracle, dev):
+def test_layer_256_experts(ckl, oracle, dev):
     _check(ckl, oracle, dev, 64, 256, 8, 256, 512)
 
 
 @pytest.mark.parametrize("T", [1, 16])
-def test_fused_config4_against_unfused(ckl, oracle, dev, T):
-    """BASELINE config 4 (E=64, top-6, d=2048, F=1408) at full size: the fused layer against
-    the unfused path over all tokens (the fp64 check on sampled tokens is in
+def test_layer_config4_against_single_gemm_path(ckl, oracle, dev, T):
+    """BASELINE config 4 (E=64, top-6, d=2048, F=1408) at full size: the layer against the
+    single-GEMM composition over all tokens (the fp64 check on sampled tokens is in
     test_moe_gpu.py)."""
     import torch
     from moe_ref import rel_rms
@@ -113,7 +110,7 @@ def test_fused_config4_against_unfused(ckl, oracle, dev, T):
     assert rel_rms(out.float().cpu().numpy(), base.float().cpu().numpy()) <= 1e-3
 
 
-def test_fused_layer_in_cuda_graph(ckl, oracle, dev):
+def test_layer_in_cuda_graph(ckl, oracle, dev):
     """Captured once, replayed with new inputs copied into the same buffers: each replay
     equals the eager call on those inputs."""
     import torch
