@@ -58,6 +58,10 @@ struct Args {
     int out_heads, head_offset;   // direct mode: row (b, h) goes to out row b*out_heads + head_offset + h
     const int2* seq_tab;          // per sequence {kv_start, chunk_base}; NULL: the uniform fields
     float scale_log2;
+    // launched early behind the previous kernel of the stream (programmatic dependent launch):
+    // 1 = wait for it before reading any input (the general case: it may have written q, the
+    // page table or the caches); 0 = the inputs are older, wait only before completing
+    int wait_first;
 };
 
 template <int G>
@@ -78,6 +82,22 @@ decode_partial_kernel(const __grid_constant__ CUtensorMap tmK,
     const int b = bh / a.Hkv, kvh = bh - b * a.Hkv;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        fence_barrier_init();
+    }
+    if (warp == CONSUMERS && lane == 0) {
+        tma_prefetch_desc(&tmK);
+        tma_prefetch_desc(&tmV);
+    }
+    __syncthreads();
+    if (a.wait_first) pdl_wait();    // the set-up above overlapped the previous kernel's tail
+    const uint64_t deadline = globaltimer() + a.timeout_ns;
+    pdl_trigger();                   // a merge launched after us may be scheduled now
+
     const int page_beg = __ldg(a.indptr + b);
     const int npages = __ldg(a.indptr + b + 1) - page_beg;
     const int seq_len = npages > 0 ? (npages - 1) * PAGE + __ldg(a.last + b) : 0;
@@ -87,27 +107,12 @@ decode_partial_kernel(const __grid_constant__ CUtensorMap tmK,
     const int p0 = kbeg / PAGE;
     const int npg = kend > kbeg ? (kend - kbeg + PAGE - 1) / PAGE : 0;
 
-    if (threadIdx.x == 0) {
-        for (int s = 0; s < STAGES; s++) {
-            mbar_init(&full[s], 1);
-            mbar_init(&empty[s], 1);
-        }
-        fence_barrier_init();
-    }
-    __syncthreads();
-    const uint64_t deadline = globaltimer() + a.timeout_ns;
-    pdl_trigger();                   // a merge launched after us may be scheduled now
-
     // consumer state (unused by the producer warp)
     HeadState<G> hs;
     const int g = lane >> 2, t = lane & 3;
 
     if (warp == CONSUMERS) {
         // ---------------------------------------------------------------- producer warp
-        if (lane == 0) {
-            tma_prefetch_desc(&tmK);
-            tma_prefetch_desc(&tmV);
-        }
         const uint64_t pol = policy_evict_first();
         int ok = 1, issued = 0;
         for (int base = 0; base < npg && ok; base += 32) {
@@ -231,6 +236,7 @@ merge_states_kernel(const float* __restrict__ part_o, const float* __restrict__ 
                     int Hq, int out_heads, int head_offset, const int2* __restrict__ seq_tab,
                     int tail) {
     pdl_wait();                      // partials of the kernel(s) before us
+    pdl_trigger();                   // the next call's kernels may start their set-up
     const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (row >= rows) return;
     const int b = row / Hq;
@@ -254,6 +260,66 @@ merge_states_kernel(const float* __restrict__ part_o, const float* __restrict__ 
             acc.z += w * v.z;
             acc.w += w * v.w;
         }
+    }
+    const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
+    __half2 h0 = __floats2half2_rn(acc.x * inv, acc.y * inv);
+    __half2 h1 = __floats2half2_rn(acc.z * inv, acc.w * inv);
+    uint2 pk;
+    pk.x = *reinterpret_cast<uint32_t*>(&h0);
+    pk.y = *reinterpret_cast<uint32_t*>(&h1);
+    reinterpret_cast<uint2*>(out + orow * D)[lane] = pk;
+    if (lane == 0) lse_out[orow] = wsum > 0.f ? m + logf(wsum) : -INFINITY;
+}
+
+// The same merge for few rows with many slots (one long sequence split into dozens of chunks):
+// one CTA per row, its 8 warps take slots c = w (mod 8) and the warps' sums are added in warp
+// order, so a row's slots are read by 8 warps in parallel instead of one walking them all.
+__global__ void __launch_bounds__(256)
+merge_states_split_kernel(const float* __restrict__ part_o, const float* __restrict__ part_lse,
+                          __half* __restrict__ out, float* __restrict__ lse_out, int rows,
+                          int stride, int Hq, int out_heads, int head_offset,
+                          const int2* __restrict__ seq_tab, int tail) {
+    __shared__ float4 s_acc[8][32];
+    __shared__ float s_w[8];
+    pdl_wait();                      // partials of the kernel(s) before us
+    pdl_trigger();                   // the next call's kernels may start their set-up
+    const int row = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int b = row / Hq;
+    const size_t orow = (size_t)b * out_heads + head_offset + row % Hq;
+    const int slots = seq_tab ? min(stride, seq_tab[b].y + tail) : stride;
+    const float* L = part_lse + (size_t)row * stride;
+    float m = -INFINITY;
+    for (int c = lane; c < slots; c += 32) m = fmaxf(m, L[c]);
+    m = warp_max(m);                 // every warp finds the same row maximum
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    float wsum = 0.f;
+    if (m != -INFINITY) {
+        const float4* po = reinterpret_cast<const float4*>(part_o + (size_t)row * stride * D) + lane;
+#pragma unroll 4
+        for (int c = warp; c < slots; c += 8) {
+            const float w = ex2((L[c] - m) * LOG2E);
+            const float4 v = po[(size_t)c * (D / 4)];
+            wsum += w;
+            acc.x += w * v.x;
+            acc.y += w * v.y;
+            acc.z += w * v.z;
+            acc.w += w * v.w;
+        }
+    }
+    s_acc[warp][lane] = acc;
+    if (lane == 0) s_w[warp] = wsum;
+    __syncthreads();
+    if (warp != 0) return;
+    acc = s_acc[0][lane];
+    wsum = s_w[0];
+#pragma unroll
+    for (int w = 1; w < 8; w++) {
+        const float4 v = s_acc[w][lane];
+        acc.x += v.x;
+        acc.y += v.y;
+        acc.z += v.z;
+        acc.w += v.w;
+        wsum += s_w[w];
     }
     const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
     __half2 h0 = __floats2half2_rn(acc.x * inv, acc.y * inv);
@@ -339,7 +405,8 @@ ckl_status validate(const ckl_decode_params* p, int* G) {
 
 ckl_status launch_partial(const ckl_decode_params* p, int G, bool direct, __half* out,
                           float* lse, float* part_o, float* part_lse, cudaStream_t stream,
-                          int out_heads, int head_offset, bool pdl, const int2* seq_tab) {
+                          int out_heads, int head_offset, bool pdl, const int2* seq_tab,
+                          bool wait_first) {
     const DeviceInfo* di = device_info();
     if (!di) return CKL_CUDA_ERROR;
     const KernelSetup* ks = setup(di);
@@ -372,6 +439,7 @@ ckl_status launch_partial(const ckl_decode_params* p, int G, bool direct, __half
     a.head_offset = head_offset;
     a.seq_tab = seq_tab;
     a.scale_log2 = p->sm_scale * LOG2E;
+    a.wait_first = wait_first ? 1 : 0;
 
     void* args[] = {&tmK, &tmV, &a};
     dim3 grid((unsigned)(p->B * p->Hkv), (unsigned)p->num_chunks);
@@ -384,6 +452,13 @@ ckl_status launch_merge(const float* part_o, const float* part_lse, __half* out,
                         const int2* seq_tab, int tail, cudaStream_t stream) {
     void* args[] = {&part_o, &part_lse, &out, &lse, &rows, &stride, &Hq, &out_heads, &head_offset,
                     &seq_tab, &tail};
+    // one warp per row unless that leaves the GPU nearly idle with long rows to walk
+    const DeviceInfo* di = device_info();
+    if (di && stride >= 16 && rows < 4 * di->sms) {
+        CKL_CUDA_TRY(launch(reinterpret_cast<const void*>(merge_states_split_kernel), dim3(rows),
+                            dim3(256), 0, stream, args, true));
+        return CKL_OK;
+    }
     CKL_CUDA_TRY(launch(reinterpret_cast<const void*>(merge_states_kernel), dim3(ceil_div(rows, 8)),
                         dim3(256), 0, stream, args, true));
     return CKL_OK;
@@ -476,7 +551,7 @@ ckl_status decode_attention_rows(const ckl_decode_params* p, void* out, float* l
     if (!out || !lse) return fail(CKL_INVALID_ARG, "out/lse are NULL");
     if (p->num_chunks == 1 && p->chunk_base == 0 && p->part_stride == 1)
         return launch_partial(p, G, true, static_cast<__half*>(out), lse, nullptr, nullptr, s,
-                              out_heads, head_offset);
+                              out_heads, head_offset, true, nullptr, true);
     const size_t need = ckl_decode_workspace_size(p);
     if (!workspace || workspace_bytes < need)
         return fail(CKL_WORKSPACE_TOO_SMALL, "decode_attention needs %zu workspace bytes, got %zu",
@@ -485,7 +560,7 @@ ckl_status decode_attention_rows(const ckl_decode_params* p, void* out, float* l
     if ((uintptr_t)out & 7) return fail(CKL_INVALID_ARG, "out needs 8-byte alignment");
     float* part_o = static_cast<float*>(workspace);
     float* part_lse = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + part_o_bytes(p));
-    st = launch_partial(p, G, false, nullptr, nullptr, part_o, part_lse, s, 0, 0);
+    st = launch_partial(p, G, false, nullptr, nullptr, part_o, part_lse, s, 0, 0, true, nullptr, true);
     if (st != CKL_OK) return st;
     return launch_merge(part_o, part_lse, static_cast<__half*>(out), lse, p->B * p->Hq, p->part_stride,
                         p->Hq, out_heads > 0 ? out_heads : p->Hq, head_offset, nullptr, 0, s);
