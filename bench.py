@@ -908,6 +908,172 @@ def bench_moe_ep(ckl, dev, timer, peak, rank, world, exchange, n_layers=8):
     return res
 
 
+def ep_a2a_layer(ckl, q, lg, X, k, world, cap):
+    """One expert-parallel MoE layer with NCCL all-to-all moving the rows: route on the
+    token's GPU, scatter the permuted rows into fixed-capacity per-owner slabs [world][cap]
+    (cap >= rows any GPU sends one owner), all_to_all_single the rows and the per-expert
+    counts, build the owner's gather map on the device (no host sync), run the owner's
+    experts (q = gate, up, down over E/world experts), send the fp32 rows back with a
+    second all_to_all_single and combine. Every GPU makes the same collective calls."""
+    import torch
+    import torch.distributed as dist
+    dev, d = X.device, X.shape[1]
+    Tr, E_loc = X.shape[0], q[0].E
+    i32 = dict(dtype=torch.int32, device=dev)
+    S = torch.zeros((world * cap, d), dtype=torch.float16, device=dev)
+    if Tr:
+        r = ckl.route_and_permute(lg, X, k)
+        rows = torch.arange(Tr * k, **i32)
+        expert = torch.searchsorted(r["offsets"], rows, right=True) - 1
+        owner = torch.div(expert, E_loc, rounding_mode="floor")
+        slot_send = owner * cap + (rows - r["offsets"][owner * E_loc])          # [Tr*k]
+        S.index_copy_(0, slot_send, r["Xp"])
+        counts = r["counts"]
+    else:
+        counts = torch.zeros(world * E_loc, **i32)
+    R = torch.empty_like(S)
+    dist.all_to_all_single(R, S)
+    cnt = torch.empty(world * E_loc, **i32)
+    dist.all_to_all_single(cnt, counts.contiguous())
+    cnt = cnt.view(world, E_loc).long()                                     # [src][expert]
+    ends = torch.cumsum(cnt, 1)                                             # per src slab
+    loc_off = torch.zeros(E_loc + 1, dtype=torch.long, device=dev)
+    loc_off[1:] = torch.cumsum(cnt.sum(0), 0)
+    before = torch.cumsum(cnt, 0) - cnt                                     # earlier srcs' rows
+    sl = torch.arange(cap, device=dev).unsqueeze(0).expand(world, cap).contiguous()
+    j = torch.searchsorted(ends, sl, right=True).clamp(max=E_loc - 1)       # expert of slot
+    src = torch.arange(world, device=dev).unsqueeze(1).expand(world, cap)
+    pos = loc_off[j] + before[src, j] + sl - (ends - cnt)[src, j]           # GEMM row of slot
+    A = world * cap
+    pos = torch.where(sl < ends[:, -1:], pos, torch.full_like(pos, A)).view(-1)   # empty -> spare
+    row_src = torch.zeros(A + 1, **i32)
+    row_src.index_copy_(0, pos, torch.arange(A, **i32))
+    off = loc_off.int()
+    h = ckl.expert_gemm_ex(R, row_src, off, A, q[0], q[1])
+    y = ckl.expert_gemm_ex(h, None, off, A, q[2], None, y_f32=True)
+    Sb = torch.cat([y, torch.zeros((1, d), dtype=torch.float32, device=dev)])[pos]
+    Rb = torch.empty_like(Sb)
+    dist.all_to_all_single(Rb, Sb)
+    if not Tr:
+        return torch.empty((0, d), dtype=torch.float16, device=dev)
+    return ckl.combine(Rb[slot_send], r["inv_perm"], r["wts"], Tr, k)
+
+
+def ep_replicated_layer(ckl, q, lg, X, k, rank, world, Tmax):
+    """One expert-parallel MoE layer with replicated tokens: X and the logits all-gathered
+    (every GPU's batch padded to Tmax rows; padding routes to some expert and is computed
+    and discarded), every GPU runs its own experts (q over E/world experts) for the rows
+    routed to them, the fp32 weighted partial outputs of all tokens are reduce-scattered
+    back to the tokens' GPUs."""
+    import torch
+    import torch.distributed as dist
+    dev, d = X.device, X.shape[1]
+    Tr, E, E_loc = X.shape[0], lg.shape[1], q[0].E
+    Xpad = torch.zeros((Tmax, d), dtype=torch.float16, device=dev)
+    Xpad[:Tr] = X
+    Lpad = torch.zeros((Tmax, E), dtype=torch.float32, device=dev)
+    Lpad[:Tr] = lg
+    T = world * Tmax
+    Xall = torch.empty((T, d), dtype=torch.float16, device=dev)
+    Lall = torch.empty((T, E), dtype=torch.float32, device=dev)
+    dist.all_gather_into_tensor(Xall, Xpad)
+    dist.all_gather_into_tensor(Lall, Lpad)
+    r = ckl.route_and_permute(Lall, Xall, k)
+    A = T * k
+    off = r["offsets"][rank * E_loc:(rank + 1) * E_loc + 1]                  # rows of my experts
+    h = ckl.expert_gemm_ex(r["Xp"], None, off, A, q[0], q[1])
+    y = ckl.expert_gemm_ex(h, None, off, A, q[2], None, y_f32=True)
+    rows = torch.arange(A, device=dev)
+    mine = ((rows >= off[0]) & (rows < off[-1])).unsqueeze(1)
+    y = torch.where(mine, y, torch.zeros((), dtype=y.dtype, device=dev))
+    part = (y[r["inv_perm"].long()].view(T, k, d) * r["wts"].unsqueeze(2)).sum(1)
+    out = torch.empty((Tmax, d), dtype=torch.float32, device=dev)
+    dist.reduce_scatter_tensor(out, part)
+    return out[:Tr].half()
+
+
+def bench_moe_ep_designs(ckl, dev, timer, peak, rank, world, exchange, n_layers=8):
+    """BASELINE config 4 expert-parallel, three ways of moving the tokens on the same local
+    expert weights (experts [r*E/n, (r+1)*E/n) on GPU r) and the same inputs, each timed as
+    n_layers layers in one CUDA graph (L2 flushed before every replay, per-layer time, max
+    over GPUs):
+      * ipc_kernels: ckl_moe_ep_layer, dispatch and combine by the layer's own kernels
+        through IPC-mapped windows (this library's design);
+      * nccl_all_to_all: ep_a2a_layer (fixed-capacity slabs, two NCCL all-to-alls);
+      * nccl_replicated_reduce_scatter: ep_replicated_layer (all-gather, reduce-scatter).
+    Each NCCL design's first-layer output is compared with the IPC layer's (relative RMS)."""
+    import torch
+    import torch.distributed as dist
+    E, k, d, F, T_cap = 64, 6, 2048, 1408, 64
+    E_loc = E // world
+    g = torch.Generator(device=dev)
+    g.manual_seed(4500 + rank)
+    mk = lambda *sh: (torch.randn(*sh, generator=g, device=dev) * 0.02).half()
+    win = ckl.EpWindows(rank, world, T_cap, k, E, d, exchange)
+    layers = []
+    for _ in range(n_layers):
+        q = [ckl.QuantWeights(4, mk(E_loc, d, F), group=128, asym=True) for _ in range(2)]
+        q.append(ckl.QuantWeights(4, mk(E_loc, F, d), group=128, asym=True))
+        layers.append((q, ckl.MoeEpLayer(win, *q)))
+    ws = torch.empty(layers[0][1].workspace_size(), dtype=torch.uint8, device=dev)
+    res = {}
+    for name, T in [("T=1", 1), ("T=16", 16), ("T=64", 64), ("T=64/GPU", 64 * world)]:
+        Tc = [_split(T, world, rr) for rr in range(world)]
+        Tr, Tmax = Tc[rank], max(Tc)
+        cap = Tmax * min(k, E_loc)
+        lg = [torch.randn((max(Tr, 1), E), generator=g, device=dev)[:Tr].contiguous()
+              for _ in range(n_layers)]
+        X = torch.randn((max(Tr, 1), d), generator=g, device=dev).half()[:Tr].contiguous()
+        outs = {}
+        ipc_out = [torch.empty((Tr, d), dtype=torch.float16, device=dev) for _ in range(n_layers)]
+
+        def step_ipc():
+            x = X
+            for l, (_, layer) in enumerate(layers):
+                layer.forward(lg[l], x, out=ipc_out[l], workspace=ws)
+                x = ipc_out[l]
+            outs["ipc_kernels"] = ipc_out[0]
+
+        def chain(key, fn):
+            def step():
+                x = X
+                for l, (q, _) in enumerate(layers):
+                    x = fn(q, lg[l], x)
+                    if l == 0:
+                        outs[key] = x
+            return step
+
+        steps = {"ipc_kernels": step_ipc,
+                 "nccl_all_to_all": chain("nccl_all_to_all", lambda q, l_, x: ep_a2a_layer(
+                     ckl, q, l_, x, k, world, cap)),
+                 "nccl_replicated_reduce_scatter": chain(
+                     "nccl_replicated_reduce_scatter",
+                     lambda q, l_, x: ep_replicated_layer(ckl, q, l_, x, k, rank, world, Tmax))}
+        row = {"tokens_per_gpu": Tr}
+        graphs = {}
+        for key, fn in steps.items():
+            graphs[key] = GraphStep(fn, dev)
+            row[key + "_us_per_layer"] = round(timer(graphs[key]) / n_layers * 1e3, 2)
+        if Tr:
+            ref = outs["ipc_kernels"].float()
+            for key in ("nccl_all_to_all", "nccl_replicated_reduce_scatter"):
+                row[key + "_rel_rms_vs_ipc"] = float(
+                    (outs[key].float() - ref).norm() / max(float(ref.norm()), 1e-30))
+        torch.cuda.synchronize()
+        del graphs, outs
+        res[name] = row
+    res["method"] = (f"{n_layers} layers with distinct weights ({E_loc} experts per GPU) in one "
+                     "CUDA graph per design and GPU, L2 flushed before each replay, per-layer "
+                     "time, max over GPUs; rel_rms: first layer's output against the IPC "
+                     "layer's, on rank 0")
+    torch.cuda.synchronize()
+    dist.barrier()
+    del layers
+    win.close()
+    torch.cuda.empty_cache()
+    return res
+
+
 def bench_mixtral_ep(ckl, dev, timer, peak, rank, world, exchange):
     """BASELINE config 5 on several GPUs: attention of B=32 sequences of 4096 with the KV
     heads sharded over the GPUs (each GPU decodes its 8/n KV heads for all sequences), then
@@ -1221,6 +1387,9 @@ def run_ours(args):
                     extras[name] = fn(ckl, dev, timer, peak)
         else:
             ex = ckl.torch_exchange()
+            if "config4_moe_ep_designs" in want:           # opt-in: NCCL designs compared
+                extras["config4_moe_ep_designs"] = bench_moe_ep_designs(ckl, dev, timer, peak, rank,
+                                                                        world, ex)
             if run("config4_moe_w4a16_layer_ep"):
                 extras["config4_moe_w4a16_layer_ep"] = bench_moe_ep(ckl, dev, timer, peak, rank,
                                                                     world, ex)

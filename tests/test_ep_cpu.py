@@ -181,3 +181,117 @@ def test_ep_window_layout_and_argument_checks(ckl):
     comm.T_cap = 4
     args_big = (None, None, 5) + args[3:]                          # T > T_cap
     assert lib.ckl_moe_ep_layer(C.byref(comm), *args_big) == 1
+
+
+class _HostOps:
+    """The library calls the NCCL expert-parallel designs of bench.py make, restated on the
+    host (routing and slot order from the oracle; the SwiGLU intermediate rounded to fp16
+    and the down projection kept in fp32, as the GPU GEMMs write them). Rows the offsets do
+    not cover stay NaN, so a design that reads one fails."""
+
+    class W:
+        def __init__(self, W):
+            self.W, self.E, self.N = W, W.shape[0], W.shape[2]
+
+    def __init__(self, oracle):
+        self.O = oracle
+
+    def route_and_permute(self, lg, X, k):
+        import torch
+        ids, wts = self.O.route(lg.numpy(), k)
+        counts, offsets, _, inv = self.O.permute(ids, lg.shape[1])
+        Xp = torch.empty((X.shape[0] * k, X.shape[1]), dtype=torch.float16)
+        Xp[torch.from_numpy(inv).long()] = X.repeat_interleave(k, 0)
+        t = lambda a: torch.from_numpy(np.ascontiguousarray(a))
+        return dict(ids=t(ids), wts=t(wts.astype(np.float32)), counts=t(counts),
+                    offsets=t(offsets), inv_perm=t(inv), Xp=Xp)
+
+    def expert_gemm_ex(self, X, row_src, offsets, A, gate, up=None, y_f32=False):
+        import torch
+        Y = torch.full((A, gate.N), float("nan"),
+                       dtype=torch.float32 if y_f32 else torch.float16)
+        off = offsets.tolist()
+        for e in range(gate.E):
+            rows = torch.arange(off[e], off[e + 1])
+            if not len(rows):
+                continue
+            x = (X[row_src[rows].long()] if row_src is not None else X[rows]).double().numpy()
+            if up is not None:
+                g, u = x @ gate.W[e], x @ up.W[e]
+                y = (g / (1 + np.exp(-g)) * u).astype(np.float16)
+            else:
+                y = (x @ gate.W[e]).astype(np.float32 if y_f32 else np.float16)
+            Y[rows] = torch.from_numpy(y)
+        return Y
+
+    def combine(self, Yp, inv_perm, wts, T, k):
+        import torch
+        y = Yp.double()[inv_perm.long()].view(T, k, -1)
+        return (y * wts.double().unsqueeze(2)).sum(1).half()
+
+
+def _designs_worker(rank, world, port, T_all, out_q):
+    import torch
+    import torch.distributed as dist
+    sys.path[:0] = [os.path.join(ROOT, "oracle"), ROOT]
+    import oracle as O
+    import bench
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                            world_size=world, timeout=timedelta(seconds=60))
+    try:
+        E, k = 8, 3
+        logits, X, mats = _problem(E=E, k=k, T_all=T_all)
+        E_loc = E // world
+        ops = _HostOps(O)
+        q = [_HostOps.W(m[rank * E_loc:(rank + 1) * E_loc]) for m in mats]
+        t0, T = sum(T_all[:rank]), T_all[rank]
+        lg = torch.from_numpy(logits[t0:t0 + T].copy())
+        x = torch.from_numpy(X[t0:t0 + T].copy())
+        Tmax = max(T_all)
+        a2a = bench.ep_a2a_layer(ops, q, lg, x, k, world, Tmax * min(k, E_loc))
+        rep = bench.ep_replicated_layer(ops, q, lg, x, k, rank, world, Tmax)
+        out_q.put((rank, a2a.float().numpy(), rep.float().numpy()))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("T_all", [(5, 3), (4, 0), (1, 1)])
+def test_nccl_ep_designs_two_ranks_match_single_process(T_all, oracle):
+    """bench.py's NCCL all-to-all and replicated + reduce-scatter expert-parallel layers (the
+    designs timed beside ckl_moe_ep_layer) on two gloo ranks against the single-process
+    layer with the same roundings."""
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_designs_worker, args=(r, 2, port, T_all, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in procs:
+        r, *rest = q.get(timeout=240)
+        res[r] = rest
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+
+    E, k = 8, 3
+    logits, X, (Wg, Wu, Wd) = _problem(E=E, k=k, T_all=T_all)
+    ids, wts = oracle.route(logits, k)
+    x = X.astype(np.float64)
+    ref = np.zeros((len(X), Wd.shape[2]))
+    for t in range(len(X)):
+        for j in range(k):
+            e = ids[t, j]
+            g, u = x[t] @ Wg[e], x[t] @ Wu[e]
+            h = (g / (1 + np.exp(-g)) * u).astype(np.float16).astype(np.float64)
+            ref[t] += wts[t, j].astype(np.float32) * (h @ Wd[e]).astype(np.float32)
+    t0 = 0
+    for r in range(2):
+        T = T_all[r]
+        for out in res[r]:
+            assert out.shape == (T, Wd.shape[2]) and np.isfinite(out).all()
+            if T:
+                err = np.abs(out - ref[t0:t0 + T]).max() / np.abs(ref).max()
+                assert err < 2e-3, err
+        t0 += T
