@@ -740,12 +740,61 @@ def bench_mixtral_layer(ckl, dev, timer, peak):
     return res
 
 
+class CublasGrouped:
+    """The reference's baseline (c), cublasGemmGroupedBatchedEx with one group per non-empty
+    expert (02_moe_grouped_gemm.cu:397-423), called through ctypes on the cuBLAS library torch
+    loads: column-major C[f x n_e] = W_e[f x d] . Xp_e[d x n_e], fp16 in and out, fp32
+    compute. The host-side arrays are built once (not timed), as the reference does. A
+    baseline leg only: never on the library's path."""
+
+    def __init__(self, Xp, W, Y, offs):
+        import ctypes as C
+        import torch
+        import nvidia.cublas
+        path = os.path.join(list(nvidia.cublas.__path__)[0], "lib", "libcublas.so.12")
+        self.L = L = C.CDLL(path)
+        self.h = C.c_void_p()
+        if L.cublasCreate_v2(C.byref(self.h)) != 0:
+            raise RuntimeError("cublasCreate failed")
+        E, d, f = W.shape
+        act = [e for e in range(E) if offs[e + 1] > offs[e]]
+        G = len(act)
+        I = C.c_int * G
+        self.keep = dict(
+            ta=I(*[0] * G), tb=I(*[0] * G), m=I(*[f] * G), n=I(*[offs[e + 1] - offs[e] for e in act]),
+            k=I(*[d] * G), lda=I(*[f] * G), ldb=I(*[d] * G), ldc=I(*[f] * G),
+            alpha=(C.c_float * G)(*[1.0] * G), beta=(C.c_float * G)(*[0.0] * G), size=I(*[1] * G))
+        ptr = lambda base, e, stride: base.data_ptr() + e * stride
+        self.pa = torch.tensor([ptr(W, e, d * f * 2) for e in act], dtype=torch.int64, device=W.device)
+        self.pb = torch.tensor([ptr(Xp, offs[e], d * 2) for e in act], dtype=torch.int64, device=W.device)
+        self.pc = torch.tensor([ptr(Y, offs[e], f * 2) for e in act], dtype=torch.int64, device=W.device)
+        self.G = G
+        L.cublasGemmGroupedBatchedEx.restype = C.c_int
+
+    def __call__(self):
+        import ctypes as C
+        import torch
+        k = self.keep
+        self.L.cublasSetStream_v2(self.h, C.c_void_p(torch.cuda.current_stream().cuda_stream))
+        vp = lambda t: C.c_void_p(t.data_ptr())
+        st = self.L.cublasGemmGroupedBatchedEx(
+            self.h, k["ta"], k["tb"], k["m"], k["n"], k["k"], k["alpha"], vp(self.pa), 2, k["lda"],
+            vp(self.pb), 2, k["ldb"], k["beta"], vp(self.pc), 2, k["ldc"], self.G, k["size"], 68)
+        if st != 0:
+            raise RuntimeError(f"cublasGemmGroupedBatchedEx status {st}")
+
+    def close(self):
+        self.L.cublasDestroy_v2(self.h)
+
+
 def bench_grouped_gemm(ckl, dev, timer, peak):
     """The dense grouped expert GEMM (ckl_moe_grouped_gemm, tcgen05) on the reference's
     performance shapes (02_moe_grouped_gemm.cu:342-344): routed and permuted once, then the
     GEMM alone with a cold L2. Bound: HBM (every shape streams more weight bytes than the
-    tensor cores need time for); both fractions are reported. Beside it, for context, the
-    reference's baseline (a): one cuBLAS GEMM per expert through torch.matmul."""
+    tensor cores need time for); both fractions are reported. Beside it the reference's
+    three cuBLAS baselines (02:367-423): (a) one GEMM per expert (torch.matmul), (b) every
+    expert padded to the largest count, one strided-batched GEMM (torch.bmm; padding copy
+    not timed), (c) cublasGemmGroupedBatchedEx (CublasGrouped)."""
     import torch
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as fh:
@@ -776,13 +825,30 @@ def bench_grouped_gemm(ckl, dev, timer, peak):
                 if offs[e + 1] > offs[e]:
                     torch.matmul(Xp[offs[e]:offs[e + 1]], W[e], out=Yp[offs[e]:offs[e + 1]])
         t_ref = timer(per_expert)
+        Yg = torch.empty_like(Yp)
+        cg = CublasGrouped(Xp, W, Yg, offs)
+        cg()
+        torch.cuda.synchronize()
+        grouped_diff = float((Yg.float() - Yp.float()).abs().max())
+        t_grouped = timer(cg)
+        cg.close()
+        max_n = max(offs[e + 1] - offs[e] for e in range(E))
+        Xpad = torch.zeros((E, max_n, d), dtype=torch.float16, device=dev)
+        for e in range(E):
+            Xpad[e, :offs[e + 1] - offs[e]] = Xp[offs[e]:offs[e + 1]]
+        Ypad = torch.empty((E, max_n, f), dtype=torch.float16, device=dev)
+        t_padded = timer(lambda: torch.bmm(Xpad, W, out=Ypad))
+        del Xpad, Ypad, Yg
         res[name] = {"us": round(t * 1e3, 1), "active_experts": active,
                      "tokens_per_expert": round(A / E, 1),
                      "GB/s": round(byts / (t * 1e-3) / 1e9, 1),
                      "frac_of_measured_hbm": round(byts / (t * 1e-3) / 1e9 / peak, 3),
                      "TFLOP/s": round(flops / (t * 1e-3) / 1e12, 1),
                      "frac_of_measured_bf16_tensor": round(flops / (t * 1e-3) / 1e12 / tf_peak, 3),
-                     "us_cublas_per_expert_loop": round(t_ref * 1e3, 1)}
+                     "us_cublas_per_expert_loop": round(t_ref * 1e3, 1),
+                     "us_cublas_padded_batched": round(t_padded * 1e3, 1),
+                     "us_cublas_grouped_batched_ex": round(t_grouped * 1e3, 1),
+                     "max_abs_diff_vs_cublas_grouped": grouped_diff}
         del W, Xp, Yp, r
         torch.cuda.empty_cache()
     res["method"] = "cold L2 (512 MB memset before each sample), median of 31; bytes = active experts' fp16 weights + Xp + Yp"
@@ -1000,7 +1066,9 @@ def bench_moe_ep_designs(ckl, dev, timer, peak, rank, world, exchange, n_layers=
       * ipc_kernels: ckl_moe_ep_layer, dispatch and combine by the layer's own kernels
         through IPC-mapped windows (this library's design);
       * nccl_all_to_all: ep_a2a_layer (fixed-capacity slabs, two NCCL all-to-alls);
-      * nccl_replicated_reduce_scatter: ep_replicated_layer (all-gather, reduce-scatter).
+      * nccl_replicated_reduce_scatter: ep_replicated_layer (all-gather, reduce-scatter);
+      * *_collectives_only: each NCCL design's collectives alone, same sizes, no compute (the
+        floor of that design whatever its glue).
     Each NCCL design's first-layer output is compared with the IPC layer's (relative RMS)."""
     import torch
     import torch.distributed as dist
@@ -1049,6 +1117,32 @@ def bench_moe_ep_designs(ckl, dev, timer, peak, rank, world, exchange, n_layers=
                  "nccl_replicated_reduce_scatter": chain(
                      "nccl_replicated_reduce_scatter",
                      lambda q, l_, x: ep_replicated_layer(ckl, q, l_, x, k, rank, world, Tmax))}
+        # the NCCL designs' collectives alone (no routing, GEMMs or glue): their floor
+        S16 = torch.zeros((world * cap, d), dtype=torch.float16, device=dev)
+        R16, S32 = torch.empty_like(S16), torch.zeros((world * cap, d), dtype=torch.float32, device=dev)
+        R32 = torch.empty_like(S32)
+        cs, cr = (torch.zeros(E, dtype=torch.int32, device=dev) for _ in range(2))
+        Xg, Lg = (torch.zeros((Tmax, n), dtype=t, device=dev) for n, t in ((d, torch.float16),
+                                                                           (E, torch.float32)))
+        Xa = torch.empty((world * Tmax, d), dtype=torch.float16, device=dev)
+        La = torch.empty((world * Tmax, E), dtype=torch.float32, device=dev)
+        P, O = torch.zeros((world * Tmax, d), dtype=torch.float32, device=dev), torch.empty(
+            (Tmax, d), dtype=torch.float32, device=dev)
+
+        def a2a_only():
+            for _ in range(n_layers):
+                dist.all_to_all_single(R16, S16)
+                dist.all_to_all_single(cr, cs)
+                dist.all_to_all_single(R32, S32)
+
+        def replicated_only():
+            for _ in range(n_layers):
+                dist.all_gather_into_tensor(Xa, Xg)
+                dist.all_gather_into_tensor(La, Lg)
+                dist.reduce_scatter_tensor(O, P)
+
+        steps["nccl_all_to_all_collectives_only"] = a2a_only
+        steps["nccl_replicated_collectives_only"] = replicated_only
         row = {"tokens_per_gpu": Tr}
         graphs = {}
         for key, fn in steps.items():
