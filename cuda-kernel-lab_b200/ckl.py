@@ -150,8 +150,10 @@ _SIGS = {
                                         C.c_void_p, C.c_void_p]),
     "ckl_moe_combine": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p,
                                   C.c_int, C.c_int, C.c_int, C.c_void_p]),
+    "ckl_moe_grouped_gemm_workspace_size": (C.c_size_t, []),
     "ckl_moe_grouped_gemm": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int,
-                                       C.c_int, C.c_int, C.c_int, C.c_void_p]),
+                                       C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_size_t,
+                                       C.c_void_p]),
     "ckl_moe_weights_save": (C.c_int, [C.c_char_p, C.POINTER(MoeWeights), C.c_void_p]),
     "ckl_moe_weights_file_info": (C.c_int, [C.c_char_p, C.POINTER(MoeWeights)]),
     "ckl_moe_weights_load": (C.c_int, [C.c_char_p, C.POINTER(MoeWeights), C.c_void_p]),
@@ -649,9 +651,27 @@ def expert_gemm_ex(X, row_src, offsets, A, gate, up=None, y_f32=False, force_ksp
     return Y
 
 
-def grouped_gemm(Xp, W, offsets, out=None, stream=None):
+_GROUPED_WS = {}
+
+
+def grouped_workspace(dev):
+    """A zeroed ckl_moe_grouped_gemm workspace for device dev (every completed launch leaves
+    its flag words zero, so it is reused; one launch at a time)."""
+    torch = _torch()
+    key = torch.device(dev).index if torch.device(dev).index is not None else torch.cuda.current_device()
+    ws = _GROUPED_WS.get(key)
+    if ws is None:
+        n = lib().ckl_moe_grouped_gemm_workspace_size()
+        if n == C.c_size_t(-1).value:
+            raise CklError(3, "ckl_moe_grouped_gemm_workspace_size", "no CUDA device")
+        ws = _GROUPED_WS[key] = torch.zeros(n, dtype=torch.uint8, device=dev)
+    return ws
+
+
+def grouped_gemm(Xp, W, offsets, out=None, workspace=None, stream=None):
     """moe_grouped_gemm (02_moe_grouped_gemm.cu:86-186): Yp[r] = Xp[r] . W[e] over the
-    expert-sorted rows, fp16 [A][f] (tcgen05). W fp16 [E][d][f]."""
+    expert-sorted rows, fp16 [A][f] (tcgen05). W fp16 [E][d][f]. workspace: a zeroed
+    ckl_moe_grouped_gemm_workspace_size() buffer (default: one cached per device)."""
     torch = _torch()
     _need(Xp, torch.float16, "Xp")
     _need(W, torch.float16, "W")
@@ -659,7 +679,10 @@ def grouped_gemm(Xp, W, offsets, out=None, stream=None):
     E, _, f = W.shape
     if out is None:
         out = torch.empty((A, f), dtype=torch.float16, device=Xp.device)
+    if workspace is None:
+        workspace = grouped_workspace(Xp.device)
     check(lib().ckl_moe_grouped_gemm(_ptr(Xp), _ptr(W), _ptr(out), _ptr(offsets), A, E, d, f,
+                                     _ptr(workspace), workspace.numel() * workspace.element_size(),
                                      _stream(stream)), "ckl_moe_grouped_gemm")
     return out
 

@@ -372,10 +372,17 @@ CKL_API ckl_status ckl_moe_combine(const void* Yp, int y_f32, const int* inv_per
  * tokens or more per expert: Yp[r] = Xp[r] . W[e] for the rows r in [offsets[e],
  * offsets[e+1]) of every expert, fp16 in, fp32 accumulation, fp16 out. Xp [A][d] sorted by
  * expert (ckl_moe_route_permute), W fp16 [E][d][f] row-major (the reference's layout),
- * offsets [E+1] device. tcgen05 tensor cores, one launch, device-side schedule (no host
- * sync). d % 64 == 0, f % 128 == 0. */
+ * offsets [E+1] device. tcgen05 tensor cores, one persistent launch, device-side schedule (no
+ * host sync). d % 64 == 0, f % 128 == 0, E <= 256.
+ * workspace: ckl_moe_grouped_gemm_workspace_size() bytes (16-byte aligned) whose first 1024
+ * bytes are zero before the first launch; every launch that completes leaves them zero (they
+ * are the flags of the k-split work items, the rest holds their fp32 partial tiles). One
+ * workspace serves one launch at a time; after a CKL_TIMEOUT (ckl_check_device_error) zero it
+ * again. */
+CKL_API size_t ckl_moe_grouped_gemm_workspace_size(void);
 CKL_API ckl_status ckl_moe_grouped_gemm(const void* Xp, const void* W, void* Yp, const int* offsets,
-                                        int A, int E, int d, int f, void* stream);
+                                        int A, int E, int d, int f, void* workspace,
+                                        size_t workspace_bytes, void* stream);
 
 /* Stable on-disk format of packed expert weights (no reference counterpart: the reference
  * quantises at start-up, 03_moe_wq_decode.cu:286-299). A 64-byte little-endian header

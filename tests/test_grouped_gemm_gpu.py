@@ -5,7 +5,8 @@ The reference's correctness cases (02:310-314, full layer: route + permute + gro
 combine) are checked against the fp64 oracle with the reference's tolerance (rtol 1e-2,
 atol 5e-3, 02:326-330); its prefill shapes (02:342-344) at full size against a fp32 torch
 GEMM per expert on the same fp16 inputs; experts with more than 256 rows (several row
-chunks), empty experts, and run-to-run bit identity."""
+chunks), empty experts, and run-to-run bit identity; the persistent stream-K schedule's
+cut items (partial tiles, flags cleared for the next launch) and its workspace check."""
 import numpy as np
 import pytest
 
@@ -79,3 +80,77 @@ def test_reference_prefill_shapes_full_size(ckl, oracle, dev, T, E, k, d, f):
         worst = max(worst, float((got - ref).abs().max()))
     del W
     torch.cuda.empty_cache()
+
+
+def _torch_ref(Xp, W, off):
+    import torch
+    Y = torch.zeros((Xp.shape[0], W.shape[2]), dtype=torch.float32, device=Xp.device)
+    for e in range(W.shape[0]):
+        a, b = int(off[e]), int(off[e + 1])
+        if b > a:
+            Y[a:b] = Xp[a:b].float() @ W[e].float()
+    return Y
+
+
+def _case(dev, T, E, k, d, f, seed):
+    import torch
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    lg = torch.randn((T, E), generator=g, device=dev)
+    X = (torch.rand((T, d), generator=g, device=dev) * 2 - 1).half()
+    W = ((torch.rand((E, d, f), generator=g, device=dev) * 2 - 1) / d ** 0.5).half()
+    return lg, X, W
+
+
+@pytest.mark.parametrize("T,E,k,d,f", [(3, 2, 1, 4096, 256), (2, 1, 1, 8192, 128),
+                                       (5, 3, 2, 2048, 384)])
+def test_items_cut_across_many_ctas(ckl, dev, T, E, k, d, f):
+    """Few items with long k: one item's k blocks are spread over up to 128 CTAs (stream-K
+    writers and one finisher), ranges of one k block, empty ranges."""
+    import torch
+    lg, X, W = _case(dev, T, E, k, d, f, seed=d + f)
+    r = ckl.route_and_permute(lg, X, k)
+    ws = ckl.grouped_workspace(dev)
+    Yp = ckl.grouped_gemm(r["Xp"], W, r["offsets"], workspace=ws)
+    torch.cuda.synchronize()
+    ckl.check_device_error()
+    ref = _torch_ref(r["Xp"], W, r["offsets"].cpu().numpy())
+    bad = (Yp.float() - ref).abs() > 5e-3 + 1e-2 * ref.abs()
+    assert int(bad.sum()) == 0, float((Yp.float() - ref).abs().max())
+    assert int(ws[:1024].count_nonzero()) == 0          # every flag cleared by its finisher
+    again = ckl.grouped_gemm(r["Xp"], W, r["offsets"], workspace=ws)
+    assert torch.equal(again, Yp)
+
+
+def test_changing_routings_reuse_one_workspace(ckl, dev):
+    """Launches with different expert counts back to back on one workspace (the flags each
+    launch leaves must be the zeros the next one needs); the first result is reproduced."""
+    import torch
+    ws = ckl.grouped_workspace(dev)
+    cases = [(64, 8, 2, 1024, 2048, 1), (300, 16, 3, 512, 1152, 2), (7, 4, 2, 2048, 512, 3)]
+    first = {}
+    for rep in range(2):
+        for T, E, k, d, f, seed in cases:
+            lg, X, W = _case(dev, T, E, k, d, f, seed)
+            r = ckl.route_and_permute(lg, X, k)
+            Yp = ckl.grouped_gemm(r["Xp"], W, r["offsets"], workspace=ws)
+            torch.cuda.synchronize()
+            ckl.check_device_error()
+            if rep == 0:
+                ref = _torch_ref(r["Xp"], W, r["offsets"].cpu().numpy())
+                bad = (Yp.float() - ref).abs() > 5e-3 + 1e-2 * ref.abs()
+                assert int(bad.sum()) == 0, (T, E, float((Yp.float() - ref).abs().max()))
+                first[seed] = Yp
+            else:
+                assert torch.equal(first[seed], Yp), (T, E)
+    assert int(ws[:1024].count_nonzero()) == 0
+
+
+def test_workspace_too_small_is_refused(ckl, dev):
+    import torch
+    lg, X, W = _case(dev, 8, 4, 2, 128, 128, seed=5)
+    r = ckl.route_and_permute(lg, X, 2)
+    small = torch.zeros(1024, dtype=torch.uint8, device=dev)
+    with pytest.raises(ckl.CklError) as ei:
+        ckl.grouped_gemm(r["Xp"], W, r["offsets"], workspace=small)
+    assert ei.value.status == ckl.CKL_WORKSPACE_TOO_SMALL
