@@ -30,119 +30,104 @@ namespace moe {
 constexpr int MAX_E = 256;
 constexpr int MAX_K = 8;
 constexpr int ROUTE_THREADS = 512;
+constexpr int ROUTE_ONE_CTA = 16;   // batches up to this many tokens route in one CTA
 constexpr int MAX_A = 4096;      // assignments one routing block handles (T * k)
 constexpr int ROUTE_SMEM_LOGITS = 6144;   // logits staged in shared memory (24 KB; with the
                                           // 18 KB of static arrays below the 48 KB default)
 
-// grid = 1, block = ROUTE_THREADS (16 warps).
-//  1. top-k, one warp per token: lane l holds logits l, l+32, ... (coalesced loads); k rounds
-//     of a warp argmax on (value, -id), so ties go to the lower id; the winner's owner marks
-//     it used. Softmax is monotonic, so top-k of the logits is top-k of p; the weights are
-//     the renormalised p: w_j = exp(l_j - l_max) / sum_j' exp(l_j' - l_max) (= p_j / sum p,
-//     common/moe.cuh:64-70).
-//  2. integer histogram (order-free), exclusive scan -> offsets (and tile offsets);
-//  3. stable rank, thread per assignment: slot = offsets[e] + #{i' < i : ids[i'] = e}.
-__global__ void __launch_bounds__(ROUTE_THREADS)
-route_kernel(const float* __restrict__ logits, int T, int E, int k, int* __restrict__ ids,
-             float* __restrict__ wts, int* __restrict__ counts, int* __restrict__ offsets,
-             int* __restrict__ inv_perm, int* __restrict__ row_src, int bm, int* __restrict__ tiles) {
-    __shared__ __align__(16) int s_ids[MAX_A];
-    __shared__ int s_cnt[MAX_E];
-    __shared__ int s_off[MAX_E + 1];
-    extern __shared__ float s_dyn[];                         // [T][E+1] logits, [T][MAX_K] picks
-    float* s_lg = s_dyn;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int A = T * k;
-    pdl_trigger();                    // the expert GEMM may launch; it waits for our results
-    for (int e = threadIdx.x; e < E; e += blockDim.x) s_cnt[e] = 0;
-    const bool staged = T * (E + 1) <= ROUTE_SMEM_LOGITS;    // the launch sized s_lg for this
-    const int lg_stride = E + 1;
-    float* s_selv = s_dyn + (staged ? (size_t)T * lg_stride : 0);   // [T][MAX_K] chosen logits
-    if (staged)                                                // one coalesced pass
-        for (int i = threadIdx.x; i < T * E; i += blockDim.x)
-            s_lg[(i / E) * lg_stride + i % E] = __ldg(logits + i);
-    __syncthreads();
-
-    // top-k, one warp per token: lane l holds experts l, l+32, ... as order-preserving keys of
-    // their logits (-0 folded into +0, so equal logits tie); k rounds of a warp argmax (max key
-    // by one reduction, then the lowest id holding it by another), the winner's key retired.
-    // This is the reference's order: larger value first, ties to the lower id
-    // (common/moe.cuh:55-59), and round r fills slot r.
-    const int nwarps = blockDim.x >> 5;
+// Top-k of one token by one warp (lane l holds experts l, l+32, ... as order-preserving keys
+// of their logits, -0 folded into +0 so equal logits tie): k rounds of a warp argmax (max key
+// by one reduction, then the lowest id holding it by another), the winner's key retired. This
+// is the reference's order: larger value first, ties to the lower id (common/moe.cuh:55-59),
+// and round r fills slot r. Softmax is monotonic, so top-k of the logits is top-k of p; the
+// weights are the renormalised p: w_j = exp(l_j - l_max) / sum_j' exp(l_j' - l_max)
+// (= p_j / sum p, common/moe.cuh:64-70). lg = the token's E logits (shared or global
+// memory); writes ids/wts of the token's k slots; s_ids / s_cnt (nullable) receive the ids
+// and the histogram.
+__device__ __forceinline__ void topk_token(const float* lg, int E, int k, int lane,
+                                           int* __restrict__ ids, float* __restrict__ wts,
+                                           int* s_ids, int* s_cnt) {
     const int nj = (E + 31) >> 5;                          // experts per lane (<= MAX_E / 32)
-    for (int t = warp; t < T; t += nwarps) {
-        const float* lg = staged ? s_lg + (size_t)t * lg_stride : logits + (size_t)t * E;
-        uint32_t key[MAX_E / 32];
+    uint32_t key[MAX_E / 32];
 #pragma unroll
-        for (int j = 0; j < MAX_E / 32; j++) {
-            const int e = lane + 32 * j;
-            uint32_t u = 0;                                // below every logit's key
-            if (j < nj && e < E) {
-                uint32_t bits = __float_as_uint(lg[e]);
-                if (bits == 0x80000000u) bits = 0u;
-                u = (bits & 0x80000000u) ? ~bits : (bits | 0x80000000u);
-            }
-            key[j] = u;
+    for (int j = 0; j < MAX_E / 32; j++) {
+        const int e = lane + 32 * j;
+        uint32_t u = 0;                                    // below every logit's key
+        if (j < nj && e < E) {
+            uint32_t bits = __float_as_uint(lg[e]);
+            if (bits == 0x80000000u) bits = 0u;
+            u = (bits & 0x80000000u) ? ~bits : (bits | 0x80000000u);
         }
-        for (int r = 0; r < k; r++) {
-            uint32_t bk = key[0];
-            int bj = 0;
-#pragma unroll
-            for (int j = 1; j < MAX_E / 32; j++) {
-                if (j >= nj) break;
-                if (key[j] > bk) { bk = key[j]; bj = j; }   // ties keep the lower id
-            }
-            const uint32_t m = __reduce_max_sync(0xffffffffu, bk);
-            const int e = (int)__reduce_min_sync(0xffffffffu, bk == m ? (uint32_t)(lane + 32 * bj) : 0xffffffffu);
-#pragma unroll
-            for (int j = 0; j < MAX_E / 32; j++)
-                if (lane + 32 * j == e) key[j] = 0u;
-            if (lane == 0) {
-                s_ids[t * k + r] = e;
-                s_selv[t * MAX_K + r] = lg[e];
-                ids[t * k + r] = e;
-                atomicAdd(&s_cnt[e], 1);                   // integer histogram: order-free
-            }
-        }
-        __syncwarp();
-        // weights renormalised over the chosen k: lane r < k owns slot r
-        float p = 0.f;
-        if (lane < k) p = expf(s_selv[t * MAX_K + lane] - s_selv[t * MAX_K]);
-        float den = p;
-#pragma unroll
-        for (int o = 1; o < MAX_K; o <<= 1) den += __shfl_xor_sync(0xffffffffu, den, o);
-        if (lane < k) wts[t * k + lane] = p * __frcp_rn(den);
+        key[j] = u;
     }
-    __syncthreads();
-    if (warp == 0) {                                       // exclusive scan over E, 32 at a time
-        int carry = 0, tcarry = 0;
-        for (int e0 = 0; e0 < E; e0 += 32) {
-            const int e = e0 + lane;
-            const int c = e < E ? s_cnt[e] : 0;
-            const int tcount = tiles && e < E ? (c + bm - 1) / bm : 0;
-            int inc = c, tinc = tcount;
+    float v0 = 0.f, vmine = 0.f;                           // round 0's logit, round lane's logit
+    for (int r = 0; r < k; r++) {
+        uint32_t bk = key[0];
+        int bj = 0;
 #pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-                const int y = __shfl_up_sync(0xffffffffu, inc, o);
-                const int ty = __shfl_up_sync(0xffffffffu, tinc, o);
-                if (lane >= o) { inc += y; tinc += ty; }
-            }
-            if (e < E) {
-                s_off[e] = carry + inc - c;
-                offsets[e] = carry + inc - c;
-                counts[e] = c;
-                if (tiles) tiles[e] = tcarry + tinc - tcount;
-            }
-            carry += __shfl_sync(0xffffffffu, inc, 31);
-            tcarry += __shfl_sync(0xffffffffu, tinc, 31);
+        for (int j = 1; j < MAX_E / 32; j++) {
+            if (j >= nj) break;
+            if (key[j] > bk) { bk = key[j]; bj = j; }       // ties keep the lower id
         }
+        const uint32_t m = __reduce_max_sync(0xffffffffu, bk);
+        const int e = (int)__reduce_min_sync(0xffffffffu, bk == m ? (uint32_t)(lane + 32 * bj) : 0xffffffffu);
+#pragma unroll
+        for (int j = 0; j < MAX_E / 32; j++)
+            if (lane + 32 * j == e) key[j] = 0u;
+        const float v = lg[e];
+        if (r == 0) v0 = v;
+        if (lane == r) vmine = v;
         if (lane == 0) {
-            s_off[E] = carry;
-            offsets[E] = carry;
-            if (tiles) tiles[E] = tcarry;
+            ids[r] = e;
+            if (s_ids) s_ids[r] = e;
+            if (s_cnt) atomicAdd(&s_cnt[e], 1);             // integer histogram: order-free
         }
     }
-    __syncthreads();
+    // weights renormalised over the chosen k: lane r < k owns slot r
+    float p = 0.f;
+    if (lane < k) p = expf(vmine - v0);
+    float den = p;
+#pragma unroll
+    for (int o = 1; o < MAX_K; o <<= 1) den += __shfl_xor_sync(0xffffffffu, den, o);
+    if (lane < k) wts[lane] = p * __frcp_rn(den);
+}
+
+// Counts, offsets (and tile offsets) from the histogram s_cnt, by warp 0: exclusive scan over
+// E, 32 at a time. Writes s_off[0..E] too.
+__device__ __forceinline__ void scan_offsets(const int* s_cnt, int* s_off, int E, int* __restrict__ counts,
+                                             int* __restrict__ offsets, int bm, int* __restrict__ tiles) {
+    const int lane = threadIdx.x & 31;
+    int carry = 0, tcarry = 0;
+    for (int e0 = 0; e0 < E; e0 += 32) {
+        const int e = e0 + lane;
+        const int c = e < E ? s_cnt[e] : 0;
+        const int tcount = tiles && e < E ? (c + bm - 1) / bm : 0;
+        int inc = c, tinc = tcount;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, inc, o);
+            const int ty = __shfl_up_sync(0xffffffffu, tinc, o);
+            if (lane >= o) { inc += y; tinc += ty; }
+        }
+        if (e < E) {
+            s_off[e] = carry + inc - c;
+            offsets[e] = carry + inc - c;
+            counts[e] = c;
+            if (tiles) tiles[e] = tcarry + tinc - tcount;
+        }
+        carry += __shfl_sync(0xffffffffu, inc, 31);
+        tcarry += __shfl_sync(0xffffffffu, tinc, 31);
+    }
+    if (lane == 0) {
+        s_off[E] = carry;
+        offsets[E] = carry;
+        if (tiles) tiles[E] = tcarry;
+    }
+}
+
+// Stable rank, thread per assignment: slot = offsets[e] + #{i' < i : ids[i'] = e}.
+__device__ __forceinline__ void rank_slots(const int* s_ids, const int* s_off, int A, int k,
+                                           int* __restrict__ inv_perm, int* __restrict__ row_src) {
     for (int i = threadIdx.x; i < A; i += blockDim.x) {
         const int e = s_ids[i];
         int r = 0, j = 0;
@@ -157,6 +142,74 @@ route_kernel(const float* __restrict__ logits, int T, int E, int k, int* __restr
         inv_perm[i] = pos;
         if (row_src) row_src[pos] = i / k;
     }
+}
+
+// grid = 1, block = ROUTE_THREADS (16 warps), for batches of up to ROUTE_ONE_CTA tokens:
+//  1. logits staged in shared memory (one coalesced pass); top-k, one warp per token;
+//  2. integer histogram (order-free), exclusive scan -> offsets (and tile offsets);
+//  3. stable rank.
+__global__ void __launch_bounds__(ROUTE_THREADS)
+route_kernel(const float* __restrict__ logits, int T, int E, int k, int* __restrict__ ids,
+             float* __restrict__ wts, int* __restrict__ counts, int* __restrict__ offsets,
+             int* __restrict__ inv_perm, int* __restrict__ row_src, int bm, int* __restrict__ tiles) {
+    __shared__ __align__(16) int s_ids[MAX_A];
+    __shared__ int s_cnt[MAX_E];
+    __shared__ int s_off[MAX_E + 1];
+    extern __shared__ float s_lg[];                           // [T][E+1] logits when they fit
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    pdl_trigger();                    // the expert GEMM may launch; it waits for our results
+    for (int e = threadIdx.x; e < E; e += blockDim.x) s_cnt[e] = 0;
+    const bool staged = T * (E + 1) <= ROUTE_SMEM_LOGITS;    // the launch sized s_lg for this
+    const int lg_stride = E + 1;
+    if (staged)
+        for (int i = threadIdx.x; i < T * E; i += blockDim.x)
+            s_lg[(i / E) * lg_stride + i % E] = __ldg(logits + i);
+    __syncthreads();
+    for (int t = warp; t < T; t += blockDim.x >> 5) {
+        const float* lg = staged ? s_lg + (size_t)t * lg_stride : logits + (size_t)t * E;
+        topk_token(lg, E, k, lane, ids + t * k, wts + t * k, s_ids + t * k, s_cnt);
+        __syncwarp();
+    }
+    __syncthreads();
+    if (warp == 0) scan_offsets(s_cnt, s_off, E, counts, offsets, bm, tiles);
+    __syncthreads();
+    rank_slots(s_ids, s_off, T * k, k, inv_perm, row_src);
+}
+
+// Larger batches in two launches, so the top-k of all tokens runs on many SMs at once:
+// route_topk_kernel (one warp per token, ROUTE_THREADS / 32 tokens per CTA) writes ids and
+// wts; route_rank_kernel (one CTA, launched behind it with PDL) builds the histogram from
+// the ids and runs the same scan and stable rank.
+__global__ void __launch_bounds__(ROUTE_THREADS)
+route_topk_kernel(const float* __restrict__ logits, int T, int E, int k, int* __restrict__ ids,
+                  float* __restrict__ wts) {
+    pdl_trigger();                    // the rank kernel may launch; it waits for our results
+    const int t = blockIdx.x * (ROUTE_THREADS / 32) + (threadIdx.x >> 5);
+    if (t < T) topk_token(logits + (size_t)t * E, E, k, threadIdx.x & 31, ids + t * k, wts + t * k,
+                          nullptr, nullptr);
+}
+
+__global__ void __launch_bounds__(ROUTE_THREADS)
+route_rank_kernel(const int* __restrict__ ids, int T, int E, int k, int* __restrict__ counts,
+                  int* __restrict__ offsets, int* __restrict__ inv_perm, int* __restrict__ row_src,
+                  int bm, int* __restrict__ tiles) {
+    __shared__ __align__(16) int s_ids[MAX_A];
+    __shared__ int s_cnt[MAX_E];
+    __shared__ int s_off[MAX_E + 1];
+    const int A = T * k;
+    for (int e = threadIdx.x; e < E; e += blockDim.x) s_cnt[e] = 0;
+    pdl_wait();                       // the top-k kernel's ids
+    pdl_trigger();                    // the expert GEMM may launch; it waits for our results
+    __syncthreads();
+    for (int i = threadIdx.x; i < A; i += blockDim.x) {
+        const int e = ids[i];
+        s_ids[i] = e;
+        atomicAdd(&s_cnt[e], 1);
+    }
+    __syncthreads();
+    if ((threadIdx.x >> 5) == 0) scan_offsets(s_cnt, s_off, E, counts, offsets, bm, tiles);
+    __syncthreads();
+    rank_slots(s_ids, s_off, A, k, inv_perm, row_src);
 }
 
 // Xp[inv_perm[i]] = X[i / k] (the reference's moe_permute copy, common/moe.cuh:90-92).
@@ -216,7 +269,7 @@ __global__ void combine_kernel(const void* __restrict__ Y, const int* __restrict
 
 inline size_t route_smem(int T, int E) {
     const size_t lgs = (size_t)T * (E + 1) <= ROUTE_SMEM_LOGITS ? (size_t)T * (E + 1) : 0;
-    return (lgs + (size_t)T * MAX_K) * sizeof(float);
+    return lgs * sizeof(float);
 }
 
 // Opt the routing kernel into up to 64 KB of dynamic shared memory, once per device.
@@ -234,15 +287,33 @@ ckl_status route_setup() {
     return st[di->device];
 }
 
+// The routing launches: one CTA up to ROUTE_ONE_CTA tokens, else top-k over many CTAs then
+// the rank CTA (PDL).
+ckl_status launch_route(const float* logits, int T, int E, int k, int* ids, float* wts,
+                        int* counts, int* offsets, int* inv_perm, int* row_src, int bm, int* tiles,
+                        cudaStream_t s) {
+    ckl_status st = route_setup();
+    if (st != CKL_OK) return st;
+    if (T <= ROUTE_ONE_CTA) {
+        route_kernel<<<1, ROUTE_THREADS, route_smem(T, E), s>>>(logits, T, E, k, ids, wts, counts,
+                                                                offsets, inv_perm, row_src, bm, tiles);
+        CKL_CUDA_TRY(cudaGetLastError());
+        return CKL_OK;
+    }
+    const int per = ROUTE_THREADS / 32;
+    route_topk_kernel<<<(T + per - 1) / per, ROUTE_THREADS, 0, s>>>(logits, T, E, k, ids, wts);
+    CKL_CUDA_TRY(cudaGetLastError());
+    const int* idsc = ids;
+    void* args[] = {&idsc, &T, &E, &k, &counts, &offsets, &inv_perm, &row_src, &bm, &tiles};
+    CKL_CUDA_TRY(launch(reinterpret_cast<const void*>(route_rank_kernel), dim3(1), dim3(ROUTE_THREADS),
+                        0, s, args, true));
+    return CKL_OK;
+}
+
 // Routing of T tokens (T may be 0: counts and offsets are then all zero).
 ckl_status route_tokens(const float* logits, int T, int E, int k, int* ids, float* wts,
                         int* counts, int* offsets, int* inv_perm, int* row_src, cudaStream_t s) {
-    ckl_status st = route_setup();
-    if (st != CKL_OK) return st;
-    route_kernel<<<1, ROUTE_THREADS, route_smem(T, E), s>>>(logits, T, E, k, ids, wts, counts,
-                                                            offsets, inv_perm, row_src, 1, nullptr);
-    CKL_CUDA_TRY(cudaGetLastError());
-    return CKL_OK;
+    return launch_route(logits, T, E, k, ids, wts, counts, offsets, inv_perm, row_src, 1, nullptr, s);
 }
 
 ckl_status check_route(int T, int E, int k) {
@@ -296,11 +367,8 @@ ckl_status ckl_moe_route_permute(const float* logits, const void* X, int T, int 
     if (Xp && (!X || d <= 0 || d % 8 || ((uintptr_t)X | (uintptr_t)Xp) & 15))
         return fail(CKL_INVALID_ARG, "moe_route_permute: X/Xp need 16-byte alignment, d%%8==0");
     const cudaStream_t s = (cudaStream_t)stream;
-    st = route_setup();
+    st = launch_route(logits, T, E, k, ids, wts, counts, offsets, inv_perm, nullptr, bm, tiles, s);
     if (st != CKL_OK) return st;
-    route_kernel<<<1, ROUTE_THREADS, route_smem(T, E), s>>>(logits, T, E, k, ids, wts, counts,
-                                                            offsets, inv_perm, nullptr, bm, tiles);
-    CKL_CUDA_TRY(cudaGetLastError());
     if (Xp) {
         permute_rows_kernel<<<T * k, 128, 0, s>>>(static_cast<const __half*>(X), inv_perm,
                                                   static_cast<__half*>(Xp), k, d);
@@ -366,11 +434,8 @@ ckl_status ckl_moe_layer(const float* logits, const void* X, int T, int k,
     const size_t split_bytes = std::max(s1, s2);
     const cudaStream_t s = (cudaStream_t)stream;
 
-    st = route_setup();
+    st = launch_route(logits, T, E, k, ids, wts, counts, offsets, inv_perm, row_src, 1, nullptr, s);
     if (st != CKL_OK) return st;
-    route_kernel<<<1, ROUTE_THREADS, route_smem(T, E), s>>>(logits, T, E, k, ids, wts, counts,
-                                                            offsets, inv_perm, row_src, 1, nullptr);
-    CKL_CUDA_TRY(cudaGetLastError());
     // gate/up waits for the routing; down prefetches its first weight stages while gate/up
     // finishes (its offsets are the routing's, one kernel older); combine waits for down.
     st = expert_gemm(X, row_src, offsets, A, T, gate, up, h, 0, 0, split, split_bytes, stream, 1);
