@@ -1058,6 +1058,59 @@ def ep_replicated_layer(ckl, q, lg, X, k, rank, world, Tmax):
     return out[:Tr].half()
 
 
+def bench_seqsplit(ckl, dev, timer, peak, rank, world, exchange, L=32768):
+    """Config 2's B=1 shape (1 x 32768) split by sequence over the GPUs: the single-GPU plan's
+    chunks cut into one run per rank, each rank holding only its run's pages and writing its
+    partial slots into rank 0's buffers (ckl_decode_partial over a peer-mapped buffer), a
+    gather signal, then rank 0's wait and LSE merge. Cold L2 on every rank, ranks start each
+    sample together, max over ranks."""
+    import numpy as np
+    import torch
+    lens = np.array([L], np.int32)
+    d, (lens, indptr, indices) = paged_batch(lens, dev, seed=7)
+    nc, ct = ckl.plan_chunks(HQ // HKV, 1, HKV, L)
+    lo, hi = rank * nc // world, (rank + 1) * nc // world
+    t0, t1 = lo * ct, min(hi * ct, L)
+    pages = torch.from_numpy(np.asarray(indices[t0 // PAGE:(t1 + PAGE - 1) // PAGE], np.int64)).to(dev)
+    kl = d["k_cache"].index_select(0, pages).contiguous()
+    vl = d["v_cache"].index_select(0, pages).contiguous()
+    del d["k_cache"], d["v_cache"]
+    n = pages.numel()
+    t = lambda a: torch.tensor(a, dtype=torch.int32, device=dev)
+    p = ckl.make_params(d["q"], kl, vl, t([0, n]), t(list(range(n))), t([t1 - t0 - (n - 1) * PAGE]),
+                        num_chunks=hi - lo, chunk_tokens=ct, chunk_base=lo, part_stride=nc)
+    o_bytes = (HQ * nc * D * 4 + 255) // 256 * 256
+    win = ckl.IpcWindows(rank, world, o_bytes + HQ * nc * 4, exchange)
+    grp = ckl.GatherGroup(rank, world, exchange)
+    p.part_o, p.part_lse = win.ptrs[0], win.ptrs[0] + o_bytes
+    out = torch.empty((1, HQ, D), dtype=torch.float16, device=dev)
+    lse = torch.empty((1, HQ), dtype=torch.float32, device=dev)
+    po = ckl.device_view(win.ptrs[0], (HQ, nc, D), torch.float32) if rank == 0 else None
+    pl = ckl.device_view(win.ptrs[0] + o_bytes, (HQ, nc), torch.float32) if rank == 0 else None
+
+    def step():
+        ckl.decode_partial(p)
+        grp.signal(0)
+        if rank == 0:
+            grp.wait()
+            ckl.merge_states(po, pl, out, lse)
+
+    ms = timer(step)
+    byts = algorithmic_bytes(lens)
+    torch.cuda.synchronize()
+    res = {"1x32768": {"us": round(ms * 1e3, 1), "chunks": nc, "chunks_per_gpu": [lo, hi],
+                       "GB/s_all_gpus": round(byts / (ms * 1e-3) / 1e9, 1),
+                       "frac_of_measured_hbm_all_gpus": round(byts / (ms * 1e-3) / 1e9 / (peak * world), 3)},
+           "method": "cold L2 (512 MB memset) on every rank, ranks start each sample together, "
+                     "median of 31, max over ranks; partial slots over NVLink into rank 0, "
+                     "gather flags, LSE merge on rank 0"}
+    win.close()
+    grp.close()
+    del kl, vl
+    torch.cuda.empty_cache()
+    return res
+
+
 def bench_moe_ep_designs(ckl, dev, timer, peak, rank, world, exchange, n_layers=8):
     """BASELINE config 4 expert-parallel, three ways of moving the tokens on the same local
     expert weights (experts [r*E/n, (r+1)*E/n) on GPU r) and the same inputs, each timed as
@@ -1481,6 +1534,9 @@ def run_ours(args):
                     extras[name] = fn(ckl, dev, timer, peak)
         else:
             ex = ckl.torch_exchange()
+            if run("config2_1x32768_seqsplit"):
+                extras["config2_1x32768_seqsplit"] = bench_seqsplit(ckl, dev, timer, peak, rank,
+                                                                    world, ex)
             if "config4_moe_ep_designs" in want:           # opt-in: NCCL designs compared
                 extras["config4_moe_ep_designs"] = bench_moe_ep_designs(ckl, dev, timer, peak, rank,
                                                                         world, ex)

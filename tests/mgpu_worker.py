@@ -5,6 +5,9 @@ Attention by KV head: each rank decodes its heads' shard and writes the rows str
 rank 0's output (ckl_decode_attention_gather over a peer-mapped buffer), signals, and rank 0
 waits (ckl_gather_wait) and compares the gathered output with the full single-GPU decode
 under the same split: a head's rows do not depend on other heads, so they must be equal.
+One long sequence (B=1) by its chunks: each rank holds only its run of the plan's chunks,
+writes those partial slots into rank 0's buffers, and rank 0 merges them (bit-identical to
+the single-GPU decode with the same plan).
 
 MoE by expert: each rank packs only its own experts, runs ckl_moe_ep_layer on its share of
 the tokens and checks the routing against the oracle, the output against the single-GPU
@@ -148,6 +151,64 @@ def attention_case(ckl, oracle, rank, world, dev, name, lens, force_chunks, exch
     return res
 
 
+def seqsplit_case(ckl, oracle, rank, world, dev, name, L, exchange):
+    """One long sequence split by its chunks over the ranks (B=1): rank r holds only the
+    pages of its chunk run [lo_r, hi_r) of the single-GPU plan, runs the partial kernel over
+    them (ckl_decode_partial with chunk_base = lo_r, part_stride = all chunks) with the
+    partial buffers in rank 0's window, signals; rank 0 waits and runs the LSE merge. The
+    slots are the single-GPU decode's slots, so the result equals it bit for bit."""
+    import torch
+    HQ, HKV, D, PAGE = 32, 8, 128, 16
+    bt = oracle.batch([L], HQ, HKV, seed=91)
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+    k_all, v_all, q = t(bt.k).view(-1, PAGE, HKV, D), t(bt.v).view(-1, PAGE, HKV, D), t(bt.q)
+    nc, ct = ckl.plan_chunks(HQ // HKV, 1, HKV, L)
+    assert nc >= world, (nc, world)
+    lo, hi = rank * nc // world, (rank + 1) * nc // world
+    t0, t1 = lo * ct, min(hi * ct, L)
+    pages = bt.indices[t0 // PAGE:(t1 + PAGE - 1) // PAGE]
+    pi = torch.from_numpy(pages.astype(np.int64)).to(dev)
+    kl, vl = k_all.index_select(0, pi).contiguous(), v_all.index_select(0, pi).contiguous()
+    n = len(pages)
+    ip = t(np.array([0, n], np.int32))
+    ix = t(np.arange(n, dtype=np.int32))
+    ls = t(np.array([t1 - t0 - (n - 1) * PAGE], np.int32))
+    p = ckl.make_params(q, kl, vl, ip, ix, ls, num_chunks=hi - lo, chunk_tokens=ct,
+                        chunk_base=lo, part_stride=nc)
+    o_bytes = (HQ * nc * D * 4 + 255) // 256 * 256
+    win = ckl.IpcWindows(rank, world, o_bytes + HQ * nc * 4, exchange)
+    grp = ckl.GatherGroup(rank, world, exchange)
+    res = {"case": name, "chunks": nc, "rank_chunks": [lo, hi]}
+    try:
+        p.part_o, p.part_lse = win.ptrs[0], win.ptrs[0] + o_bytes
+        out = torch.empty((1, HQ, D), dtype=torch.float16, device=dev)
+        lse = torch.empty((1, HQ), dtype=torch.float32, device=dev)
+        for _ in range(2):                                   # the epochs advance per call
+            ckl.decode_partial(p)
+            grp.signal(0)
+            if rank == 0:
+                grp.wait()
+                po = ckl.device_view(win.ptrs[0], (HQ, nc, D), torch.float32)
+                pl = ckl.device_view(win.ptrs[0] + o_bytes, (HQ, nc), torch.float32)
+                ckl.merge_states(po, pl, out, lse)
+        torch.cuda.synchronize()
+        ckl.check_device_error()
+        if rank == 0:
+            ref, ref_lse = ckl.decode_attention(q, k_all, v_all, t(bt.indptr), t(bt.indices),
+                                                t(bt.last), num_chunks=nc, chunk_tokens=ct)
+            torch.cuda.synchronize()
+            assert torch.equal(out, ref), "sequence-split out differs from the single-GPU decode"
+            assert torch.equal(lse, ref_lse), "sequence-split lse differs"
+            ora = oracle.attention_ref(bt)
+            res["max_abs_vs_fp64"] = float(np.abs(out.float().cpu().numpy() - ora[0]).max())
+            assert res["max_abs_vs_fp64"] <= 2e-3, res
+    finally:
+        torch.cuda.synchronize()
+        win.close()
+        grp.close()
+    return res
+
+
 def main():
     import torch
     import torch.distributed as dist
@@ -164,6 +225,7 @@ def main():
                               [1000, 777], 3, ex))
     out.append(attention_case(ckl, oracle, rank, world, dev, "attn_64x1024_direct",
                               [1024] * 64, 1, ex))
+    out.append(seqsplit_case(ckl, oracle, rank, world, dev, "attn_B1_seqsplit_8000", 8000, ex))
     T4 = [64] * world
     out.append(case(ckl, oracle, rank, world, dev, "config4_T64_per_rank", 64, 6, 2048, 1408, 4, T4, ex))
     ragged = [(5 * r + 1) % 17 for r in range(world)]

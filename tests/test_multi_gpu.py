@@ -1,6 +1,7 @@
 """Multi-GPU paths: runs tests/mgpu_worker.py under torchrun, one process per GPU (2, or up
 to 8 with CKL_EP_TEST_GPUS), and requires every rank's result file. Attention by KV head
-with the fused gather must equal the single-GPU decode exactly (rank 0 checks); the
+with the fused gather, and one long sequence split by chunks over the GPUs with rank 0's
+LSE merge, must equal the single-GPU decode exactly (rank 0 checks); the
 expert-parallel MoE layer must match the single-GPU layer and a fp32 reference (within
 1e-3 and 1e-2 relative RMS; each rank checks its own tokens). Skipped with fewer than 2
 GPUs."""
@@ -41,8 +42,8 @@ def test_head_parallel_attention_and_expert_parallel_moe(tmp_path):
         with open(tmp_path / f"rank{rank}.json") as f:
             res = json.load(f)
         assert [c["case"] for c in res] == ["attn_config1_3chunks", "attn_64x1024_direct",
-                                            "config4_T64_per_rank", "config4_ragged",
-                                            "config5_T32"]
+                                            "attn_B1_seqsplit_8000", "config4_T64_per_rank",
+                                            "config4_ragged", "config5_T32"]
         for c in res:
             if "rel_rms_vs_fp32" in c:
                 assert c["rel_rms_vs_fp32"] <= 1e-2 and c["rel_rms_vs_single_gpu"] < 1e-3, c
