@@ -239,6 +239,20 @@ __device__ __forceinline__ bool consume_pass(const GemmArgs& a, const uint8_t* r
 __device__ __forceinline__ void consumer_bar() {
     asm volatile("bar.sync 1, %0;" ::"n"(CONSUMERS * 32) : "memory");
 }
+// The same barrier returning the AND of pred over the consumer warps, so that a bounded wait
+// that gave up in one warp sends every consumer warp out together (none is left at a barrier).
+__device__ __forceinline__ bool consumer_bar_and(bool pred) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 p, %1, 0;\n\t"
+        "barrier.red.and.pred q, 1, %2, p;\n\t"
+        "selp.u32 %0, 1, 0, q;\n\t}"
+        : "=r"(r)
+        : "r"((uint32_t)pred), "n"(CONSUMERS * 32)
+        : "memory");
+    return r != 0;
+}
 
 // grid = (quads, min(E, A) expert slots, ksplit); 9 warps (8 consumers + 1 producer).
 template <int BITS, bool SWIGLU, bool GROUPED, int OCC>
@@ -370,13 +384,11 @@ moe_gemm_kernel(const GemmArgs a) {
         const bool ok = ntl == 1
             ? consume_pass<BITS, SWIGLU, GROUPED, OCC, 1>(a, ring, full, empty, seq, nst, g_beg, g_end, deadline, acc0, acc1)
             : consume_pass<BITS, SWIGLU, GROUPED, OCC, TMAX>(a, ring, full, empty, seq, nst, g_beg, g_end, deadline, acc0, acc1);
-        if (!__all_sync(0xffffffffu, ok)) return;          // timed out (already recorded)
-
         // the two warps of a tile hold partial sums over alternate groups: add them
         // [value][tile][lane]: consecutive lanes hit consecutive banks
         float* rw = red + tile * 32 + lane;
         constexpr int RS = TILES * 32;
-        if (half == 1) {
+        if (half == 1 && ok) {
 #pragma unroll
             for (int i = 0; i < TMAX; i++)
 #pragma unroll
@@ -385,7 +397,7 @@ moe_gemm_kernel(const GemmArgs a) {
                     if (SWIGLU) rw[(TMAX * 4 + i * 4 + c) * RS] = acc1[i][c];
                 }
         }
-        consumer_bar();
+        if (!consumer_bar_and(ok)) return;                // a wait timed out (already recorded)
         if (half == 0) {
             const int row0 = row_beg + r0;
 #pragma unroll
