@@ -937,6 +937,7 @@ def bench_moe_ep(ckl, dev, timer, peak, rank, world, exchange, n_layers=8):
     res = {}
     for name, T in [("T=1", 1), ("T=4", 4), ("T=16", 16), ("T=64", 64), ("T=64/GPU", 64 * world)]:
         Tr = _split(T, world, rank)
+        T_max = _split(T, world, 0)                      # tokens on the busiest rank
         lg = [torch.randn((max(Tr, 1), E), generator=g, device=dev)[:Tr].contiguous()
               for _ in range(n_layers)]
         X = torch.randn((max(Tr, 1), d), generator=g, device=dev).half()[:Tr].contiguous()
@@ -946,7 +947,7 @@ def bench_moe_ep(ckl, dev, timer, peak, rank, world, exchange, n_layers=8):
         def step():
             x = X
             for l, (_, layer) in enumerate(layers):
-                layer.forward(lg[l], x, out=outs[l], ids=ids[l], workspace=ws)
+                layer.forward(lg[l], x, out=outs[l], ids=ids[l], workspace=ws, T_max=T_max)
                 x = outs[l]
 
         t = timer(GraphStep(step, dev)) / n_layers
@@ -1151,7 +1152,7 @@ def bench_moe_ep_designs(ckl, dev, timer, peak, rank, world, exchange, n_layers=
         def step_ipc():
             x = X
             for l, (_, layer) in enumerate(layers):
-                layer.forward(lg[l], x, out=ipc_out[l], workspace=ws)
+                layer.forward(lg[l], x, out=ipc_out[l], workspace=ws, T_max=Tmax)
                 x = ipc_out[l]
             outs["ipc_kernels"] = ipc_out[0]
 
@@ -1272,7 +1273,7 @@ def bench_mixtral_ep(ckl, dev, timer, peak, rank, world, exchange):
                              workspace=a_ws)
 
     def moe():
-        layer.forward(lg, X, out=out, ids=ids, workspace=ws)
+        layer.forward(lg, X, out=out, ids=ids, workspace=ws, T_max=_split(B, world, 0))
 
     def step():
         attn()

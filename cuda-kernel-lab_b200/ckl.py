@@ -179,6 +179,10 @@ _SIGS = {
                                    C.POINTER(MoeWeights), C.POINTER(MoeWeights),
                                    C.POINTER(MoeWeights), C.c_void_p, C.c_void_p, C.c_void_p,
                                    C.c_void_p, C.c_size_t, C.c_void_p]),
+    "ckl_moe_ep_layer_ex": (C.c_int, [C.POINTER(MoeEpComm), C.c_int, C.c_void_p, C.c_void_p,
+                                      C.c_int, C.POINTER(MoeWeights), C.POINTER(MoeWeights),
+                                      C.POINTER(MoeWeights), C.c_void_p, C.c_void_p, C.c_void_p,
+                                      C.c_void_p, C.c_size_t, C.c_void_p]),
 }
 
 
@@ -883,7 +887,10 @@ class MoeEpLayer:
         return lib().ckl_moe_ep_workspace_size(C.byref(self.win.comm), C.byref(self.gate.w),
                                                C.byref(self.down.w))
 
-    def forward(self, logits, X, out=None, ids=None, wts=None, workspace=None, stream=None):
+    def forward(self, logits, X, out=None, ids=None, wts=None, workspace=None, stream=None,
+                T_max=0):
+        """T_max: an upper bound of the tokens on every rank this call (0: T_cap), which
+        sizes the expert GEMMs' grids (ckl_moe_ep_layer_ex)."""
         torch = _torch()
         T = X.shape[0]
         dev = X.device
@@ -892,9 +899,9 @@ class MoeEpLayer:
         need = self.workspace_size()
         if workspace is None or workspace.numel() * workspace.element_size() < need:
             workspace = torch.empty(need, dtype=torch.uint8, device=dev)
-        check(lib().ckl_moe_ep_layer(C.byref(self.win.comm), _ptr(logits), _ptr(X), T,
-                                     C.byref(self.gate.w), C.byref(self.up.w),
-                                     C.byref(self.down.w), _ptr(out), _ptr(ids), _ptr(wts),
-                                     _ptr(workspace), workspace.numel() * workspace.element_size(),
-                                     _stream(stream)), "ckl_moe_ep_layer")
+        check(lib().ckl_moe_ep_layer_ex(C.byref(self.win.comm), T_max, _ptr(logits), _ptr(X), T,
+                                        C.byref(self.gate.w), C.byref(self.up.w),
+                                        C.byref(self.down.w), _ptr(out), _ptr(ids), _ptr(wts),
+                                        _ptr(workspace), workspace.numel() * workspace.element_size(),
+                                        _stream(stream)), "ckl_moe_ep_layer_ex")
         return out

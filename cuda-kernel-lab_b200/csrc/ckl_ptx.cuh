@@ -12,7 +12,7 @@ namespace ckl {
 // Bits of the device-side error word (its address is passed to every kernel that waits);
 // a bounded wait that gives up ORs a code in and the kernel returns.
 // ckl_check_device_error() reads and clears it.
-enum : unsigned { DEVERR_TIMEOUT = 1u };
+enum : unsigned { DEVERR_TIMEOUT = 1u, DEVERR_BOUND = 2u };   // a wait gave up; a caller bound was exceeded
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));

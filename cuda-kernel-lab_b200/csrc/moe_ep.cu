@@ -118,7 +118,8 @@ ep_dispatch_kernel(const EpArgs p, const __half* __restrict__ X, const int* __re
 // grid = 1: waits for every source, then the expert offsets over the received rows
 // (expert-major, then source, then slab order) and the gather map row_src[a] = slab index.
 __global__ void __launch_bounds__(RECV_THREADS)
-ep_receive_kernel(const EpArgs p, int* __restrict__ offsets_loc, int* __restrict__ row_src) {
+ep_receive_kernel(const EpArgs p, int* __restrict__ offsets_loc, int* __restrict__ row_src,
+                  int rows_bound) {
     // world * E_loc = E <= EP_MAX_E entries, indexed [s][e]
     __shared__ int s_cnt[EP_MAX_E];    // rows of (s, e), clamped to the slab
     __shared__ int s_soff[EP_MAX_E];   // slab offset of (s, e)
@@ -177,7 +178,16 @@ ep_receive_kernel(const EpArgs p, int* __restrict__ offsets_loc, int* __restrict
             if (e < p.E_loc) s_off[e] = carry + inc - c;
             carry += __shfl_sync(0xffffffffu, inc, 31);
         }
-        if (lane == 0) s_off[p.E_loc] = carry;
+        __syncwarp();
+        if (lane == 0) {
+            if (carry > rows_bound) {                 // more rows than the caller's bound: none
+                atomicOr(p.err, DEVERR_BOUND);        // is processed (offsets all zero)
+                for (int e = 0; e <= p.E_loc; e++) s_off[e] = 0;
+                for (int e = 0; e < p.world * p.E_loc; e++) s_cnt[e] = 0;
+            } else {
+                s_off[p.E_loc] = carry;
+            }
+        }
     }
     __syncthreads();
     for (int e = threadIdx.x; e <= p.E_loc; e += blockDim.x) offsets_loc[e] = s_off[e];
@@ -356,8 +366,19 @@ ckl_status ckl_moe_ep_layer(const ckl_moe_ep_comm* comm, const float* logits, co
                             const ckl_moe_weights* gate, const ckl_moe_weights* up,
                             const ckl_moe_weights* down, void* out, int* ids_out, float* wts_out,
                             void* workspace, size_t workspace_bytes, void* stream) {
+    return ckl_moe_ep_layer_ex(comm, 0, logits, X, T, gate, up, down, out, ids_out, wts_out, workspace,
+                               workspace_bytes, stream);
+}
+
+ckl_status ckl_moe_ep_layer_ex(const ckl_moe_ep_comm* comm, int T_max, const float* logits,
+                               const void* X, int T, const ckl_moe_weights* gate,
+                               const ckl_moe_weights* up, const ckl_moe_weights* down, void* out,
+                               int* ids_out, float* wts_out, void* workspace,
+                               size_t workspace_bytes, void* stream) {
     ckl_status st = check_comm(comm);
     if (st != CKL_OK) return st;
+    if (T_max < 0 || T_max > comm->T_cap)
+        return fail(CKL_INVALID_ARG, "moe_ep_layer: T_max=%d outside [0, T_cap=%d]", T_max, comm->T_cap);
     if (!gate || !up || !down) return fail(CKL_INVALID_ARG, "moe_ep_layer: NULL weights");
     const EpLayout L = ep_layout(comm->world, comm->T_cap, comm->k, comm->E, comm->d);
     const int d = comm->d, F = gate->N, k = comm->k;
@@ -367,6 +388,10 @@ ckl_status ckl_moe_ep_layer(const ckl_moe_ep_comm* comm, const float* logits, co
                     L.E_loc, d, L.E_loc, d);
     if (T < 0 || T > comm->T_cap)
         return fail(CKL_INVALID_ARG, "moe_ep_layer: T=%d outside [0, T_cap=%d]", T, comm->T_cap);
+    if (T_max > 0 && T > T_max)
+        return fail(CKL_INVALID_ARG, "moe_ep_layer: T=%d above this call's T_max=%d", T, T_max);
+    // rows any rank can receive this call: the GEMM grids' bound
+    const int A_bound = T_max > 0 ? comm->world * T_max * std::min(k, L.E_loc) : L.A_max;
     if (T > 0 && (!logits || !X || !out)) return fail(CKL_INVALID_ARG, "moe_ep_layer: NULL tensor");
     if (((uintptr_t)X | (uintptr_t)out) & 15)
         return fail(CKL_INVALID_ARG, "moe_ep_layer: X/out need 16-byte alignment");
@@ -418,15 +443,16 @@ ckl_status ckl_moe_ep_layer(const ckl_moe_ep_comm* comm, const float* logits, co
                             dim3(256), 0, s, args, true));
     }
     {
-        void* args[] = {&p, &offsets_loc, &row_src};
+        int bound = A_bound;
+        void* args[] = {&p, &offsets_loc, &row_src, &bound};
         CKL_CUDA_TRY(launch(reinterpret_cast<const void*>(ep_receive_kernel), dim3(1),
                             dim3(RECV_THREADS), 0, s, args, true));
     }
     const int* a_rows = offsets_loc + L.E_loc;
-    st = expert_gemm(own + L.rows, row_src, offsets_loc, L.A_max, comm->T_cap * comm->world, gate,
+    st = expert_gemm(own + L.rows, row_src, offsets_loc, A_bound, comm->T_cap * comm->world, gate,
                      up, h, 0, 0, split, split_bytes, stream, 1, nullptr, a_rows);
     if (st != CKL_OK) return st;
-    st = expert_gemm(h, nullptr, offsets_loc, L.A_max, comm->T_cap * comm->world, down, nullptr,
+    st = expert_gemm(h, nullptr, offsets_loc, A_bound, comm->T_cap * comm->world, down, nullptr,
                      own + L.y, 1, 0, split, split_bytes, stream, s2 > 0 ? 1 : 2, row_src, a_rows);
     if (st != CKL_OK) return st;
     {

@@ -142,7 +142,10 @@ ckl_status ckl_check_device_error(void) {
     if (v) {
         e = cudaMemcpyToSymbol(g_device_error, &zero, sizeof zero);
         if (e != cudaSuccess) return cuda_status(e, "cudaMemcpyToSymbol(g_device_error)");
-        return fail(CKL_TIMEOUT, "a kernel gave up on a bounded wait (device error 0x%x)", v);
+        if (v & DEVERR_TIMEOUT)
+            return fail(CKL_TIMEOUT, "a kernel gave up on a bounded wait (device error 0x%x)", v);
+        return fail(CKL_INVALID_ARG, "a device-side bound given by the caller was exceeded "
+                    "(device error 0x%x)", v);
     }
     return CKL_OK;
 }

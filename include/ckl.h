@@ -59,7 +59,9 @@ CKL_API const char* ckl_version(void);
 
 /* Reads and clears the device-side error word that bounded waits inside the kernels set
  * when they give up (host; synchronises the current device). Returns CKL_TIMEOUT if a
- * kernel launched since the last call timed out waiting on a barrier, else CKL_OK. */
+ * kernel launched since the last call timed out waiting on a barrier, CKL_INVALID_ARG if a
+ * device-side bound given by the caller was exceeded (ckl_moe_ep_layer_ex's T_max), else
+ * CKL_OK. */
 CKL_API ckl_status ckl_check_device_error(void);
 
 /* Upper bound, in nanoseconds, on any single spin-wait inside the library's kernels
@@ -498,6 +500,17 @@ CKL_API ckl_status ckl_moe_ep_layer(const ckl_moe_ep_comm* comm, const float* lo
                                     const ckl_moe_weights* up, const ckl_moe_weights* down,
                                     void* out, int* ids_out, float* wts_out, void* workspace,
                                     size_t workspace_bytes, void* stream);
+
+/* ckl_moe_ep_layer with T_max, an upper bound of T on every rank for this call (0 < T_max <=
+ * T_cap; 0 = T_cap). It bounds the rows a rank can receive (world * T_max * min(k, E/world)),
+ * which sizes the expert GEMMs' grids: with small batches most of the T_cap-sized grid
+ * would be CTAs that find no expert and exit. A rank that receives more rows than the bound
+ * processes none of them and records CKL_INVALID_ARG (ckl_check_device_error). */
+CKL_API ckl_status ckl_moe_ep_layer_ex(const ckl_moe_ep_comm* comm, int T_max, const float* logits,
+                                       const void* X, int T, const ckl_moe_weights* gate,
+                                       const ckl_moe_weights* up, const ckl_moe_weights* down,
+                                       void* out, int* ids_out, float* wts_out, void* workspace,
+                                       size_t workspace_bytes, void* stream);
 
 /* ======================================================================================
  * Measurement

@@ -88,6 +88,11 @@ def case(ckl, oracle, rank, world, dev, name, E, k, d, F, bits, T_all, exchange)
         ckl.check_device_error()
         assert torch.equal(out, outs[0]), "graph replay differs"
         del graph
+        # the per-call token bound (ckl_moe_ep_layer_ex) sizes the grids; same result
+        bounded = layer.forward(lg, X, T_max=max(T_all))
+        torch.cuda.synchronize()
+        ckl.check_device_error()
+        assert torch.equal(bounded, outs[0]), "T_max-bounded layer differs"
         if Tr:
             rids, _ = oracle.route(lg.cpu().numpy(), k)
             assert np.array_equal(ids.cpu().numpy(), rids), "routing"

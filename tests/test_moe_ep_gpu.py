@@ -150,3 +150,36 @@ def test_wait_gives_up_on_a_flag_nothing_sets(ckl, dev):
     finally:
         torch.cuda.synchronize()
         win.close()
+
+
+def test_world1_token_bound(ckl, dev):
+    """ckl_moe_ep_layer_ex: with T_max the GEMM grids are sized for world * T_max * min(k,
+    E_loc) rows; the output equals the unbounded layer's. A bound below the rows a rank
+    actually receives is refused on the host when it is the rank's own T, and recorded on
+    the device (CKL_INVALID_ARG from ckl_check_device_error) when it is another rank's."""
+    import torch
+    E, k, d, F, T_cap = 64, 6, 2048, 1408, 64
+    gq, uq, dq = _weights(ckl, dev, E, d, F, 4, seed=11)
+    win = _one_rank(ckl, T_cap, k, E, d)
+    try:
+        layer = ckl.MoeEpLayer(win, gq, uq, dq)
+        g = torch.Generator(device=dev)
+        g.manual_seed(12)
+        for T in (1, 4, 16):
+            lg = torch.randn((T, E), generator=g, device=dev)
+            X = torch.randn((T, d), generator=g, device=dev).half()
+            ref = layer.forward(lg, X)
+            got = layer.forward(lg, X, T_max=T)
+            torch.cuda.synchronize()
+            ckl.check_device_error()
+            assert torch.equal(got, ref), T
+        with pytest.raises(ckl.CklError) as ei:            # T above this call's bound
+            layer.forward(lg, X, T_max=T - 1)
+        assert ei.value.status == 1
+        with pytest.raises(ckl.CklError):                   # bound above the capacity
+            layer.forward(lg, X, T_max=T_cap + 1)
+        torch.cuda.synchronize()
+        ckl.check_device_error()                            # nothing recorded by the refusals
+    finally:
+        torch.cuda.synchronize()
+        win.close()
