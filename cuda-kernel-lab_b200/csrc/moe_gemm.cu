@@ -43,7 +43,7 @@ constexpr int ring_bytes(int occ) { return occ == 3 ? 64 * 1024 : 96 * 1024; }
 constexpr int XSTRIDE = GPS * 256 + 64;      // smem bytes per staged token row (pad: the two
                                              // rows a quarter-warp reads land on disjoint banks)
 constexpr int MAX_STAGES = 16;
-constexpr int TMAX = 2;                      // token tiles (8 rows each) per pass
+constexpr int TMAX = 2;                      // token tiles (8 rows each) per pass, at most
 
 // int4 fragment decode to (q - z) in fp16, exact: z of column g (zc0 = half2(1024+z)) and
 // of column g+8 (zc1n = -half2(64+z)); nibble order in moe_common.cuh. 9 instructions on
@@ -120,7 +120,9 @@ __device__ __forceinline__ int nth_active_expert(const int* offsets, int E, int 
     return -1;
 }
 
-template <int BITS, bool SWIGLU, bool GROUPED, int OCC>
+// TM: token tiles per pass (2, or 1 when no expert can have more than 16 rows: the lighter
+// kernel keeps its registers and runs ~5 % faster there).
+template <int BITS, bool SWIGLU, bool GROUPED, int OCC, int TM = TMAX>
 struct Cfg {
     static constexpr int MATS = SWIGLU ? 2 : 1;
     static constexpr bool EMBED = embeds_params(BITS, GROUPED ? KGROUP_STAGE : 0);
@@ -128,22 +130,22 @@ struct Cfg {
     static constexpr int REC = CODE + (EMBED ? PARAM_BYTES : 0);
     static constexpr int GBLK = TILES * REC;                       // one group of one matrix
     static constexpr int WBYTES = MATS * GPS * GBLK;               // weights per stage
-    static constexpr int XROWS = TMAX * 8;
+    static constexpr int XROWS = TM * 8;
     static constexpr int SBYTES = (WBYTES + XROWS * XSTRIDE + 127) / 128 * 128;
     static constexpr int STAGES_RAW = ring_bytes(OCC) / SBYTES;
     static constexpr int STAGES = STAGES_RAW > MAX_STAGES ? MAX_STAGES : STAGES_RAW;
-    static constexpr int RVALS = TMAX * 4 * MATS;                  // fp32 values per lane
+    static constexpr int RVALS = TM * 4 * MATS;                    // fp32 values per lane
     static constexpr int RED = TILES * 32 * RVALS * 4;              // cross-warp reduction
     static constexpr int SMEM = 128 + STAGES * SBYTES + RED + 2 * MAX_STAGES * 8;
 };
 
 // Consumer pass over all stages for `NT` token tiles; returns false on a timeout.
-template <int BITS, bool SWIGLU, bool GROUPED, int OCC, int NT>
+template <int BITS, bool SWIGLU, bool GROUPED, int OCC, int NT, int TM>
 __device__ __forceinline__ bool consume_pass(const GemmArgs& a, const uint8_t* ring, uint64_t* full,
                                              uint64_t* empty, int& seq, int nst, int g_beg,
                                              int g_end, uint64_t deadline,
-                                             float (&acc0)[TMAX][4], float (&acc1)[TMAX][4]) {
-    using C = Cfg<BITS, SWIGLU, GROUPED, OCC>;
+                                             float (&acc0)[TM][4], float (&acc1)[TM][4]) {
+    using C = Cfg<BITS, SWIGLU, GROUPED, OCC, TM>;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
     const int tile = warp % TILES, half = warp / TILES;
     constexpr int SPC = 16 / bytes_per_lane(BITS);         // k16 steps per 16-byte lane chunk
@@ -255,10 +257,10 @@ __device__ __forceinline__ bool consumer_bar_and(bool pred) {
 }
 
 // grid = (quads, min(E, A) expert slots, ksplit); 9 warps (8 consumers + 1 producer).
-template <int BITS, bool SWIGLU, bool GROUPED, int OCC>
+template <int BITS, bool SWIGLU, bool GROUPED, int OCC, int TM>
 __global__ void __launch_bounds__(GTHREADS, OCC)
 moe_gemm_kernel(const GemmArgs a) {
-    using C = Cfg<BITS, SWIGLU, GROUPED, OCC>;
+    using C = Cfg<BITS, SWIGLU, GROUPED, OCC, TM>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* ring = align_ptr<128>(smem_raw);
     float* red = reinterpret_cast<float*>(ring + C::STAGES * C::SBYTES);
@@ -376,32 +378,32 @@ moe_gemm_kernel(const GemmArgs a) {
     for (int p = 0; p < npass; p++) {
         const int r0 = p * C::XROWS, nr = min(C::XROWS, n_e - r0);
         const int ntl = (nr + 7) / 8;                     // token tiles in use (warp-uniform)
-        float acc0[TMAX][4], acc1[TMAX][4];
+        float acc0[TM][4], acc1[TM][4];
 #pragma unroll
-        for (int i = 0; i < TMAX; i++)
+        for (int i = 0; i < TM; i++)
 #pragma unroll
             for (int c = 0; c < 4; c++) acc0[i][c] = acc1[i][c] = 0.f;
         const bool ok = ntl == 1
-            ? consume_pass<BITS, SWIGLU, GROUPED, OCC, 1>(a, ring, full, empty, seq, nst, g_beg, g_end, deadline, acc0, acc1)
-            : consume_pass<BITS, SWIGLU, GROUPED, OCC, TMAX>(a, ring, full, empty, seq, nst, g_beg, g_end, deadline, acc0, acc1);
+            ? consume_pass<BITS, SWIGLU, GROUPED, OCC, 1, TM>(a, ring, full, empty, seq, nst, g_beg, g_end, deadline, acc0, acc1)
+            : consume_pass<BITS, SWIGLU, GROUPED, OCC, TM, TM>(a, ring, full, empty, seq, nst, g_beg, g_end, deadline, acc0, acc1);
         // the two warps of a tile hold partial sums over alternate groups: add them
         // [value][tile][lane]: consecutive lanes hit consecutive banks
         float* rw = red + tile * 32 + lane;
         constexpr int RS = TILES * 32;
         if (half == 1 && ok) {
 #pragma unroll
-            for (int i = 0; i < TMAX; i++)
+            for (int i = 0; i < TM; i++)
 #pragma unroll
                 for (int c = 0; c < 4; c++) {
                     rw[(i * 4 + c) * RS] = acc0[i][c];
-                    if (SWIGLU) rw[(TMAX * 4 + i * 4 + c) * RS] = acc1[i][c];
+                    if (SWIGLU) rw[(TM * 4 + i * 4 + c) * RS] = acc1[i][c];
                 }
         }
         if (!consumer_bar_and(ok)) return;                // a wait timed out (already recorded)
         if (half == 0) {
             const int row0 = row_beg + r0;
 #pragma unroll
-            for (int i = 0; i < TMAX; i++) {
+            for (int i = 0; i < TM; i++) {
                 if (i >= ntl) break;
 #pragma unroll
                 for (int c = 0; c < 4; c++) {
@@ -409,7 +411,7 @@ moe_gemm_kernel(const GemmArgs a) {
                     const int col = (c & 2) ? col_hi : col_lo;
                     if (r >= nr || col >= a.N) continue;
                     float v0 = (acc0[i][c] + rw[(i * 4 + c) * RS]) * ((c & 2) ? pc0_hi : pc0_lo);
-                    float v1 = SWIGLU ? (acc1[i][c] + rw[(TMAX * 4 + i * 4 + c) * RS]) * ((c & 2) ? pc1_hi : pc1_lo) : 0.f;
+                    float v1 = SWIGLU ? (acc1[i][c] + rw[(TM * 4 + i * 4 + c) * RS]) * ((c & 2) ? pc1_hi : pc1_lo) : 0.f;
                     if (a.ksplit > 1) {
                         const size_t o = (size_t)(row0 + r) * a.N + col;
                         float* P = static_cast<float*>(a.Y) + (size_t)blockIdx.z * a.A * a.N * C::MATS;
@@ -671,10 +673,17 @@ struct Variant {
     int smem;
 };
 #define CKL_V(B, SW, GR, OCC) \
-    Variant{reinterpret_cast<KernelFn>(moe_gemm_kernel<B, SW, GR, OCC>), Cfg<B, SW, GR, OCC>::SMEM}
+    Variant{reinterpret_cast<KernelFn>(moe_gemm_kernel<B, SW, GR, OCC, TMAX>), Cfg<B, SW, GR, OCC>::SMEM}
+#define CKL_V1(SW, OCC) \
+    Variant{reinterpret_cast<KernelFn>(moe_gemm_kernel<4, SW, true, OCC, 1>), Cfg<4, SW, true, OCC, 1>::SMEM}
 // 3 CTAs per SM only for int4 (its stages fit twice in 64 KB; measured faster past one wave
 // of 2). The int8 and fp16 stages are 1.6-2.4x larger: at 64 KB a ring would hold one stage.
-Variant gemm_variant(int bits, bool swiglu, bool grouped, int occ) {
+// tm = 1: one token tile per pass (int4 only; for batches where no expert can have more
+// than 16 rows).
+Variant gemm_variant(int bits, bool swiglu, bool grouped, int occ, int tm = TMAX) {
+    if (bits == 4 && tm == 1)
+        return occ == 3 ? (swiglu ? CKL_V1(true, 3) : CKL_V1(false, 3))
+                        : (swiglu ? CKL_V1(true, 2) : CKL_V1(false, 2));
     if (bits == 4)
         return occ == 3 ? (swiglu ? CKL_V(4, true, true, 3) : CKL_V(4, false, true, 3))
                         : (swiglu ? CKL_V(4, true, true, 2) : CKL_V(4, false, true, 2));
@@ -685,6 +694,7 @@ Variant gemm_variant(int bits, bool swiglu, bool grouped, int occ) {
     return swiglu ? CKL_V(16, true, false, 2) : CKL_V(16, false, false, 2);
 }
 #undef CKL_V
+#undef CKL_V1
 bool gemm_occ3(int bits) { return bits == 4; }
 
 ckl_status gemm_setup(const DeviceInfo* di) {
@@ -697,12 +707,15 @@ ckl_status gemm_setup(const DeviceInfo* di) {
             for (int sw = 0; sw < 2; sw++)
                 for (int gr = 0; gr < 2; gr++) {
                     if (occ == 3 && !gemm_occ3(bits)) continue;
-                    const Variant v = gemm_variant(bits, sw, gr, occ);
-                    cudaError_t e = cudaFuncSetAttribute(
-                        v.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, v.smem);
-                    if (e != cudaSuccess) {
-                        st[di->device] = cuda_status(e, "moe gemm setup");
-                        return;
+                    for (int tm = 1; tm <= TMAX; tm++) {
+                        if (tm == 1 && bits != 4) continue;
+                        const Variant v = gemm_variant(bits, sw, gr, occ, tm);
+                        cudaError_t e = cudaFuncSetAttribute(
+                            v.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, v.smem);
+                        if (e != cudaSuccess) {
+                            st[di->device] = cuda_status(e, "moe gemm setup");
+                            return;
+                        }
                     }
                 }
     });
@@ -873,7 +886,9 @@ ckl_status expert_gemm(const void* X, const int* row_src, const int* offsets, in
         return fail(CKL_WORKSPACE_TOO_SMALL, "moe_expert_gemm needs %zu workspace bytes, got %zu",
                     need, workspace_bytes);
     const bool grouped = embeds_params(w0->bits, w0->group);   // int4, or int8 group 128
-    (void)max_rows;   // passes of up to 16 rows; the tile count is chosen per pass on the device
+    // one token tile per pass when no expert can have more than 16 rows (int4): a lighter
+    // kernel; otherwise passes of up to 16 rows
+    const int tm = (w0->bits == 4 && grouped && max_rows <= 16) ? 1 : TMAX;
     GemmArgs a;
     a.X = static_cast<const __half*>(X);
     a.row_src = row_src;
@@ -897,7 +912,7 @@ ckl_status expert_gemm(const void* X, const int* row_src, const int* offsets, in
     // 3 CTAs per SM (64 KB rings) when the grid is more than one wave of 2 (int4), else the
     // deeper rings of 2 CTAs per SM
     const int occ = gemm_occ3(w0->bits) && (long long)quads * slots * ks > 2LL * di->sms ? 3 : 2;
-    const Variant v = gemm_variant(w0->bits, swiglu, grouped, occ);
+    const Variant v = gemm_variant(w0->bits, swiglu, grouped, occ, tm);
     dim3 grid((unsigned)quads, (unsigned)slots, (unsigned)ks);
     const cudaStream_t s = (cudaStream_t)stream;
     CKL_CUDA_TRY(launch(v.fn, grid, dim3(GTHREADS), v.smem, s, args, dep != 0));
