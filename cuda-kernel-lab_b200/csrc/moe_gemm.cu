@@ -101,22 +101,28 @@ struct GemmArgs {
     int dep;
 };
 
-// The j-th expert (in id order) that has rows, or -1. Every lane returns the same value.
-__device__ __forceinline__ int nth_active_expert(const int* offsets, int E, int j) {
+// The j-th expert (in id order) that has rows, or -1; its rows [row_beg, row_beg + n_e) come
+// from the offsets the search already loaded. Every lane returns the same values.
+__device__ __forceinline__ int nth_active_expert(const int* offsets, int E, int j, int& row_beg,
+                                                 int& n_e) {
     const int lane = threadIdx.x & 31;
     int seen = 0;
     for (int e0 = 0; e0 < E; e0 += 32) {
         const int e = e0 + lane;
-        const bool act = e < E && __ldg(offsets + e + 1) > __ldg(offsets + e);
-        const unsigned m = __ballot_sync(0xffffffffu, act);
+        const int lo = e < E ? __ldg(offsets + e) : 0, hi = e < E ? __ldg(offsets + e + 1) : 0;
+        const unsigned m = __ballot_sync(0xffffffffu, hi > lo);
         const int c = __popc(m);
         if (seen + c > j) {
             unsigned mm = m;
             for (int r = j - seen; r > 0; r--) mm &= mm - 1;
-            return e0 + __ffs(mm) - 1;
+            const int src = __ffs(mm) - 1;
+            row_beg = __shfl_sync(0xffffffffu, lo, src);
+            n_e = __shfl_sync(0xffffffffu, hi, src) - row_beg;
+            return e0 + src;
         }
         seen += c;
     }
+    row_beg = n_e = 0;
     return -1;
 }
 
@@ -131,31 +137,38 @@ struct Cfg {
     static constexpr int GBLK = TILES * REC;                       // one group of one matrix
     static constexpr int WBYTES = MATS * GPS * GBLK;               // weights per stage
     static constexpr int XROWS = TM * 8;
-    static constexpr int SBYTES = (WBYTES + XROWS * XSTRIDE + 127) / 128 * 128;
-    static constexpr int STAGES_RAW = ring_bytes(OCC) / SBYTES;
-    static constexpr int STAGES = STAGES_RAW > MAX_STAGES ? MAX_STAGES : STAGES_RAW;
+    static constexpr int RING = ring_bytes(OCC);
+    // Ring layout whose stages hold the weights and XT 8-row token tiles: a CTA whose expert
+    // has at most 8 rows takes XT = 1, the deeper ring of smaller stages.
+    template <int XT>
+    struct Ring {
+        static constexpr int SB = (WBYTES + XT * 8 * XSTRIDE + 127) / 128 * 128;
+        static constexpr int N = RING / SB > MAX_STAGES ? MAX_STAGES : RING / SB;
+        static_assert(N >= 1, "ring too small for one stage");
+    };
     static constexpr int RVALS = TM * 4 * MATS;                    // fp32 values per lane
     static constexpr int RED = TILES * 32 * RVALS * 4;              // cross-warp reduction
-    static constexpr int SMEM = 128 + STAGES * SBYTES + RED + 2 * MAX_STAGES * 8;
+    static constexpr int SMEM = 128 + RING + RED + 2 * MAX_STAGES * 8;
 };
 
 // Consumer pass over all stages for `NT` token tiles; returns false on a timeout.
-template <int BITS, bool SWIGLU, bool GROUPED, int OCC, int NT, int TM>
+template <int BITS, bool SWIGLU, bool GROUPED, int OCC, int NT, int TM, int XT>
 __device__ __forceinline__ bool consume_pass(const GemmArgs& a, const uint8_t* ring, uint64_t* full,
                                              uint64_t* empty, int& seq, int nst, int g_beg,
                                              int g_end, uint64_t deadline,
                                              float (&acc0)[TM][4], float (&acc1)[TM][4]) {
     using C = Cfg<BITS, SWIGLU, GROUPED, OCC, TM>;
+    using R = typename C::template Ring<XT>;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
     const int tile = warp % TILES, half = warp / TILES;
     constexpr int SPC = 16 / bytes_per_lane(BITS);         // k16 steps per 16-byte lane chunk
     for (int si = 0; si < nst; si++, seq++) {
-        const int s = seq % C::STAGES;
-        const bool got = mbar_wait(&full[s], (seq / C::STAGES) & 1, deadline, a.err);
+        const int s = seq % R::N;
+        const bool got = mbar_wait(&full[s], (seq / R::N) & 1, deadline, a.err);
         if (!__all_sync(0xffffffffu, got)) return false;
         const int grp = g_beg + si * GPS + half;
         if (grp < g_end) {
-            const uint8_t* st = ring + (size_t)s * C::SBYTES;
+            const uint8_t* st = ring + (size_t)s * R::SB;
             const uint8_t* rec0 = st + half * C::GBLK + tile * C::REC;
             const uint8_t* rec1 = rec0 + GPS * C::GBLK;
             const uint8_t* xs = st + C::WBYTES + (size_t)g * XSTRIDE + half * 256 + 16 * t;
@@ -256,40 +269,21 @@ __device__ __forceinline__ bool consumer_bar_and(bool pred) {
     return r != 0;
 }
 
-// grid = (quads, min(E, A) expert slots, ksplit); 9 warps (8 consumers + 1 producer).
-template <int BITS, bool SWIGLU, bool GROUPED, int OCC, int TM>
-__global__ void __launch_bounds__(GTHREADS, OCC)
-moe_gemm_kernel(const GemmArgs a) {
+// The CTA's work once its expert is known: the producer warp streams the ring, warps 0-7
+// consume it. XT: 8-row token tiles a stage holds (the ring layout Cfg::Ring<XT>).
+template <int BITS, bool SWIGLU, bool GROUPED, int OCC, int TM, int XT>
+__device__ __forceinline__ void gemm_body(const GemmArgs& a, uint8_t* ring, float* red,
+                                          uint64_t* full, uint64_t* empty, int e, int row_beg,
+                                          int n_e) {
     using C = Cfg<BITS, SWIGLU, GROUPED, OCC, TM>;
-    extern __shared__ uint8_t smem_raw[];
-    uint8_t* ring = align_ptr<128>(smem_raw);
-    float* red = reinterpret_cast<float*>(ring + C::STAGES * C::SBYTES);
-    uint64_t* full = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(red) + C::RED);
-    uint64_t* empty = full + MAX_STAGES;
+    using R = typename C::template Ring<XT>;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int quad = blockIdx.x;
-
-    if (a.dep == 1) pdl_wait();                          // offsets come from the previous kernel
-    const int e = nth_active_expert(a.offsets, a.E, blockIdx.y);
-    if (e < 0) {                                         // surplus slot of the upper bound
-        pdl_trigger();
-        return;
-    }
-    const int row_beg = __ldg(a.offsets + e), n_e = __ldg(a.offsets + e + 1) - row_beg;
     const int ngroups = a.K / KGROUP_STAGE;
     const int per = (ngroups + a.ksplit - 1) / a.ksplit;
     const int g_beg = min(ngroups, (int)blockIdx.z * per), g_end = min(ngroups, g_beg + per);
     const int nst = (g_end - g_beg + GPS - 1) / GPS;     // stages per pass
     const int npass = (n_e + C::XROWS - 1) / C::XROWS;
-
-    if (threadIdx.x == 0) {
-        for (int s = 0; s < C::STAGES; s++) {
-            mbar_init(&full[s], 1);
-            mbar_init(&empty[s], CONSUMERS);
-        }
-        fence_barrier_init();
-    }
-    __syncthreads();
     const uint64_t deadline = globaltimer() + a.timeout_ns;
     if (a.dep != 2) pdl_trigger();
 
@@ -301,14 +295,18 @@ moe_gemm_kernel(const GemmArgs a) {
         const uint8_t* w0 = a.W0 + block_offset(BITS, lgroup, a.K, a.N, e, quad, 0);
         const uint8_t* w1 = SWIGLU ? a.W1 + block_offset(BITS, lgroup, a.K, a.N, e, quad, 0) : nullptr;
         // dep 2: the weights of the first stages do not depend on the previous kernel --
-        // start streaming them, then wait for it before any token row is read
+        // start streaming them, then wait for it before any token row is read. (Issuing
+        // them ahead of the row-index reads when nothing is waited for, dep 0/1, measured
+        // slower at T = 4-16: the small token-row copies then queue behind the burst.)
+        // Every prefetched stage gets its arrival in pass 0 (no wait precedes stage R::N),
+        // so no copy is left unaccounted for at exit.
         int npre = 0;
         if (a.dep == 2) {
-            npre = min(C::STAGES, nst);
+            npre = min(R::N, nst);
             if (lane == 0)
                 for (int si = 0; si < npre; si++) {
                     const int grp = g_beg + si * GPS, ngs = min(GPS, g_end - grp);
-                    uint8_t* st = ring + (size_t)si * C::SBYTES;
+                    uint8_t* st = ring + (size_t)si * R::SB;
                     mbar_expect_tx(&full[si], C::MATS * ngs * C::GBLK);
                     bulk_load(st, w0 + (size_t)grp * C::GBLK, ngs * C::GBLK, &full[si], wpol);
                     if (SWIGLU)
@@ -324,12 +322,12 @@ moe_gemm_kernel(const GemmArgs a) {
                                                       : row_beg + r0 + lane) : 0;
             const __half* xsrc = a.X + (size_t)my_src * a.K;
             for (int si = 0; si < nst; si++, seq++) {
-                const int s = seq % C::STAGES;
-                if (lane == 0 && seq >= C::STAGES)
-                    ok = mbar_wait(&empty[s], ((seq / C::STAGES) - 1) & 1, deadline, a.err);
+                const int s = seq % R::N;
+                if (lane == 0 && seq >= R::N)            // the slot's previous lap was consumed
+                    ok = mbar_wait(&empty[s], ((seq / R::N) - 1) & 1, deadline, a.err);
                 ok = __shfl_sync(0xffffffffu, ok, 0);
                 if (!ok) break;
-                uint8_t* st = ring + (size_t)s * C::SBYTES;
+                uint8_t* st = ring + (size_t)s * R::SB;
                 const int grp = g_beg + si * GPS;
                 const int ngs = min(GPS, g_end - grp);
                 if (lane == 0) {
@@ -351,9 +349,9 @@ moe_gemm_kernel(const GemmArgs a) {
         // every issued copy must land before the CTA exits
         if (lane == 0) {
             const int issued = seq;
-            for (int s = 0; s < C::STAGES && s < issued; s++) {
-                const int i_last = s + ((issued - 1 - s) / C::STAGES) * C::STAGES;
-                mbar_wait(&full[s], (i_last / C::STAGES) & 1, deadline, a.err);
+            for (int s = 0; s < R::N && s < issued; s++) {
+                const int i_last = s + ((issued - 1 - s) / R::N) * R::N;
+                mbar_wait(&full[s], (i_last / R::N) & 1, deadline, a.err);
             }
         }
         return;
@@ -384,8 +382,8 @@ moe_gemm_kernel(const GemmArgs a) {
 #pragma unroll
             for (int c = 0; c < 4; c++) acc0[i][c] = acc1[i][c] = 0.f;
         const bool ok = ntl == 1
-            ? consume_pass<BITS, SWIGLU, GROUPED, OCC, 1, TM>(a, ring, full, empty, seq, nst, g_beg, g_end, deadline, acc0, acc1)
-            : consume_pass<BITS, SWIGLU, GROUPED, OCC, TM, TM>(a, ring, full, empty, seq, nst, g_beg, g_end, deadline, acc0, acc1);
+            ? consume_pass<BITS, SWIGLU, GROUPED, OCC, 1, TM, XT>(a, ring, full, empty, seq, nst, g_beg, g_end, deadline, acc0, acc1)
+            : consume_pass<BITS, SWIGLU, GROUPED, OCC, XT, TM, XT>(a, ring, full, empty, seq, nst, g_beg, g_end, deadline, acc0, acc1);
         // the two warps of a tile hold partial sums over alternate groups: add them
         // [value][tile][lane]: consecutive lanes hit consecutive banks
         float* rw = red + tile * 32 + lane;
@@ -433,6 +431,40 @@ moe_gemm_kernel(const GemmArgs a) {
         }
         consumer_bar();                                    // red is reused by the next pass
     }
+}
+
+
+// grid = (quads, min(E, A) expert slots, ksplit); 9 warps (8 consumers + 1 producer).
+template <int BITS, bool SWIGLU, bool GROUPED, int OCC, int TM>
+__global__ void __launch_bounds__(GTHREADS, OCC)
+moe_gemm_kernel(const GemmArgs a) {
+    using C = Cfg<BITS, SWIGLU, GROUPED, OCC, TM>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* ring = align_ptr<128>(smem_raw);
+    float* red = reinterpret_cast<float*>(ring + C::RING);
+    uint64_t* full = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(red) + C::RED);
+    uint64_t* empty = full + MAX_STAGES;
+
+    if (a.dep == 1) pdl_wait();                          // offsets come from the previous kernel
+    int row_beg, n_e;
+    const int e = nth_active_expert(a.offsets, a.E, blockIdx.y, row_beg, n_e);
+    if (e < 0) {                                         // surplus slot of the upper bound
+        pdl_trigger();
+        return;
+    }
+    if (threadIdx.x == 0) {                              // enough for either ring layout
+        for (int s = 0; s < C::template Ring<1>::N; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], CONSUMERS);
+        }
+        fence_barrier_init();
+    }
+    __syncthreads();
+    // stages sized for the CTA's largest pass: one 8-row token tile, or TM
+    if (TM == 1 || n_e <= 8)
+        gemm_body<BITS, SWIGLU, GROUPED, OCC, TM, 1>(a, ring, red, full, empty, e, row_beg, n_e);
+    else
+        gemm_body<BITS, SWIGLU, GROUPED, OCC, TM, TM>(a, ring, red, full, empty, e, row_beg, n_e);
 }
 
 // Fixed-order sum of split-K partials [ksplit][A][N] (x2 for SwiGLU: gate then up); SwiGLU
