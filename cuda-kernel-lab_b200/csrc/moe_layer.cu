@@ -157,8 +157,9 @@ route_kernel(const float* __restrict__ logits, int T, int E, int k, int* __restr
     __shared__ int s_off[MAX_E + 1];
     extern __shared__ float s_lg[];                           // [T][E+1] logits when they fit
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    pdl_trigger();                    // the expert GEMM may launch; it waits for our results
     for (int e = threadIdx.x; e < E; e += blockDim.x) s_cnt[e] = 0;
+    pdl_wait();                       // launched early behind the previous kernel: its logits
+    pdl_trigger();                    // the expert GEMM may launch; it waits for our results
     const bool staged = T * (E + 1) <= ROUTE_SMEM_LOGITS;    // the launch sized s_lg for this
     const int lg_stride = E + 1;
     if (staged)
@@ -183,6 +184,7 @@ route_kernel(const float* __restrict__ logits, int T, int E, int k, int* __restr
 __global__ void __launch_bounds__(ROUTE_THREADS)
 route_topk_kernel(const float* __restrict__ logits, int T, int E, int k, int* __restrict__ ids,
                   float* __restrict__ wts) {
+    pdl_wait();                       // launched early behind the previous kernel: its logits
     pdl_trigger();                    // the rank kernel may launch; it waits for our results
     const int t = blockIdx.x * (ROUTE_THREADS / 32) + (threadIdx.x >> 5);
     if (t < T) topk_token(logits + (size_t)t * E, E, k, threadIdx.x & 31, ids + t * k, wts + t * k,
@@ -228,6 +230,7 @@ template <bool F32>
 __global__ void combine_kernel(const void* __restrict__ Y, const int* __restrict__ inv_perm,
                                const float* __restrict__ wts, __half* __restrict__ out, int k, int f) {
     pdl_wait();
+    pdl_trigger();                    // the next kernel (the next layer's routing) may launch
     const int t = blockIdx.x;
     // the k (row, weight) pairs first, so the row loads below do not wait on them one by one
     int pos_j[MAX_K];
@@ -294,15 +297,19 @@ ckl_status launch_route(const float* logits, int T, int E, int k, int* ids, floa
                         cudaStream_t s) {
     ckl_status st = route_setup();
     if (st != CKL_OK) return st;
+    // both routing launches may start behind the previous kernel of the stream (programmatic
+    // dependent launch) and wait for it before reading anything
     if (T <= ROUTE_ONE_CTA) {
-        route_kernel<<<1, ROUTE_THREADS, route_smem(T, E), s>>>(logits, T, E, k, ids, wts, counts,
-                                                                offsets, inv_perm, row_src, bm, tiles);
-        CKL_CUDA_TRY(cudaGetLastError());
+        void* args[] = {&logits, &T, &E, &k, &ids, &wts, &counts, &offsets, &inv_perm, &row_src,
+                        &bm, &tiles};
+        CKL_CUDA_TRY(launch(reinterpret_cast<const void*>(route_kernel), dim3(1), dim3(ROUTE_THREADS),
+                            route_smem(T, E), s, args, true));
         return CKL_OK;
     }
     const int per = ROUTE_THREADS / 32;
-    route_topk_kernel<<<(T + per - 1) / per, ROUTE_THREADS, 0, s>>>(logits, T, E, k, ids, wts);
-    CKL_CUDA_TRY(cudaGetLastError());
+    void* targs[] = {&logits, &T, &E, &k, &ids, &wts};
+    CKL_CUDA_TRY(launch(reinterpret_cast<const void*>(route_topk_kernel), dim3((T + per - 1) / per),
+                        dim3(ROUTE_THREADS), 0, s, targs, true));
     const int* idsc = ids;
     void* args[] = {&idsc, &T, &E, &k, &counts, &offsets, &inv_perm, &row_src, &bm, &tiles};
     CKL_CUDA_TRY(launch(reinterpret_cast<const void*>(route_rank_kernel), dim3(1), dim3(ROUTE_THREADS),
