@@ -229,17 +229,20 @@ __global__ void permute_rows_kernel(const __half* __restrict__ X, const int* __r
 template <bool F32>
 __global__ void combine_kernel(const void* __restrict__ Y, const int* __restrict__ inv_perm,
                                const float* __restrict__ wts, __half* __restrict__ out, int k, int f) {
-    pdl_wait();
-    pdl_trigger();                    // the next kernel (the next layer's routing) may launch
     const int t = blockIdx.x;
-    // the k (row, weight) pairs first, so the row loads below do not wait on them one by one
+    // The k (row, weight) pairs first, so the row loads below do not wait on them one by one.
+    // They come from the routing, which completed before the kernel we wait for was launched
+    // (the layer's chain; a standalone call is an ordinary launch): read them from L2 before
+    // the wait, so that only the rows are left for after it.
     int pos_j[MAX_K];
     float w_j[MAX_K];
 #pragma unroll
     for (int j = 0; j < MAX_K; j++) {
-        pos_j[j] = j < k ? __ldg(inv_perm + t * k + j) : 0;
-        w_j[j] = j < k ? __ldg(wts + t * k + j) : 0.f;
+        pos_j[j] = j < k ? __ldcg(inv_perm + t * k + j) : 0;
+        w_j[j] = j < k ? __ldcg(wts + t * k + j) : 0.f;
     }
+    pdl_wait();                       // the rows Y
+    pdl_trigger();                    // the next kernel (the next layer's routing) may launch
     for (int c = threadIdx.x; c < f / 8; c += blockDim.x) {
         float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
 #pragma unroll
