@@ -440,7 +440,10 @@ def bench_decode_multilayer(ckl, dev, timer, peak):
     cache, layer l's output [B, Hq, 128] is layer l+1's q (a real dependency), all captured in
     one CUDA graph and replayed with a cold L2 (512 MB memset before each replay); the figure
     is per layer. Consecutive calls overlap only their launch and set-up (the partial kernel
-    starts behind the previous merge and waits for it before reading anything)."""
+    starts behind the previous merge and waits for it before reading anything); the
+    `cache_ready` figure is the same chain through ckl_decode_attention_ex with
+    CKL_DECODE_CACHE_READY, whose producer warp reads the page table and streams the first
+    pages before that wait (the caches here are written before the step, as in decode)."""
     import torch
     rows = {}
     for name in ("1x32768", "8x8192", "64x1024", "256x4096", "ragged256"):
@@ -454,19 +457,25 @@ def bench_decode_multilayer(ckl, dev, timer, peak):
         lses = [torch.empty((len(lens), HQ), dtype=torch.float32, device=dev) for _ in range(n)]
         q0 = layers[0]["q"]
 
-        def step():
-            x = q0
-            for l, d in enumerate(layers):
-                dd = dict(d)
-                dd["q"] = x
-                ckl.decode_attention(**dd, num_chunks=nc, chunk_tokens=ct, out=outs[l], lse=lses[l],
-                                     workspace=ws)
-                x = outs[l]
+        def chain(ready):
+            def step():
+                x = q0
+                for l, d in enumerate(layers):
+                    dd = dict(d)
+                    dd["q"] = x
+                    ckl.decode_attention(**dd, num_chunks=nc, chunk_tokens=ct, out=outs[l],
+                                         lse=lses[l], workspace=ws, cache_ready=ready)
+                    x = outs[l]
+            return step
 
-        ms = timer(GraphStep(step, dev)) / n
+        ms = timer(GraphStep(chain(False), dev)) / n
+        ms_r = timer(GraphStep(chain(True), dev)) / n
         gbs = algorithmic_bytes(lens) / (ms * 1e-3) / 1e9
+        gbs_r = algorithmic_bytes(lens) / (ms_r * 1e-3) / 1e9
         rows[name] = {"layers": n, "ms_per_layer": round(ms, 4), "GB/s": round(gbs, 1),
-                      "frac_of_measured_hbm": round(gbs / peak, 3), "chunks": nc}
+                      "frac_of_measured_hbm": round(gbs / peak, 3), "chunks": nc,
+                      "cache_ready": {"ms_per_layer": round(ms_r, 4), "GB/s": round(gbs_r, 1),
+                                      "frac_of_measured_hbm": round(gbs_r / peak, 3)}}
         del layers, outs, lses, ws
         torch.cuda.empty_cache()
     rows["method"] = ("n layers with distinct KV caches in one CUDA graph, each layer's output "

@@ -25,6 +25,7 @@ PAGE = 16
 
 CKL_OK = 0
 CKL_WORKSPACE_TOO_SMALL = 6
+CKL_DECODE_CACHE_READY = 1     # ckl_decode_attention_ex flag (see include/ckl.h)
 STATUS = {0: "CKL_OK", 1: "CKL_INVALID_ARG", 2: "CKL_UNSUPPORTED_SHAPE", 3: "CKL_CUDA_ERROR",
           4: "CKL_NCCL_ERROR", 5: "CKL_TIMEOUT", 6: "CKL_WORKSPACE_TOO_SMALL"}
 
@@ -102,6 +103,8 @@ _SIGS = {
                                    C.c_int, C.c_void_p]),
     "ckl_decode_attention": (C.c_int, [C.POINTER(DecodeParams), C.c_void_p, C.c_void_p,
                                        C.c_void_p, C.c_size_t, C.c_void_p]),
+    "ckl_decode_attention_ex": (C.c_int, [C.POINTER(DecodeParams), C.c_void_p, C.c_void_p,
+                                          C.c_void_p, C.c_size_t, C.c_uint, C.c_void_p]),
     "ckl_decode_balanced_workspace_size": (C.c_size_t, [C.POINTER(DecodeParams)]),
     "ckl_decode_attention_balanced": (C.c_int, [C.POINTER(DecodeParams), C.c_void_p, C.c_void_p,
                                                 C.c_void_p, C.c_size_t, C.c_void_p]),
@@ -312,11 +315,14 @@ def merge_states(part_o, part_lse, out, lse, stream=None):
 
 def decode_attention(q, k_cache, v_cache, kv_indptr, kv_indices, kv_last_page_len, *,
                      max_len=None, force_chunks=0, num_chunks=None, chunk_tokens=None,
-                     out=None, lse=None, workspace=None, sm_scale=None, stream=None):
+                     out=None, lse=None, workspace=None, sm_scale=None, stream=None,
+                     cache_ready=False):
     """decode_attention (01_decode_attention.cu:316-331): returns (out fp16 [B,Hq,128],
     lse fp32 [B,Hq]). Plans the split like the reference (plan_chunks) unless num_chunks /
     chunk_tokens are given; max_len defaults to the longest sequence (read from the page
-    table on the host, which synchronises)."""
+    table on the host, which synchronises). cache_ready: ckl_decode_attention_ex with
+    CKL_DECODE_CACHE_READY (the page table and all but each sequence's last page were written
+    before the stream's previous kernel began)."""
     torch = _torch()
     B, Hq, _ = q.shape
     Hkv = k_cache.shape[2]
@@ -338,8 +344,13 @@ def decode_attention(q, k_cache, v_cache, kv_indptr, kv_indices, kv_last_page_le
     if need and (workspace is None or workspace.numel() * workspace.element_size() < need):
         workspace = torch.empty(need, dtype=torch.uint8, device=q.device)
     ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
-    check(lib().ckl_decode_attention(C.byref(p), _ptr(out), _ptr(lse), _ptr(workspace),
-                                     ws_bytes, _stream(stream)), "ckl_decode_attention")
+    if cache_ready:
+        check(lib().ckl_decode_attention_ex(C.byref(p), _ptr(out), _ptr(lse), _ptr(workspace),
+                                            ws_bytes, CKL_DECODE_CACHE_READY, _stream(stream)),
+              "ckl_decode_attention_ex")
+    else:
+        check(lib().ckl_decode_attention(C.byref(p), _ptr(out), _ptr(lse), _ptr(workspace),
+                                         ws_bytes, _stream(stream)), "ckl_decode_attention")
     return out, lse
 
 

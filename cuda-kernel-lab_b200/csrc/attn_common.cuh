@@ -209,12 +209,13 @@ ckl_status validate(const ckl_decode_params* p, int* G);
 // out_heads / head_offset place direct-mode rows (b, h) at b*out_heads + head_offset + h
 // (out_heads 0 = Hq). seq_tab (device, per sequence {kv_start, chunk_base}) overrides the
 // uniform p->kv_start / p->chunk_base of partial-mode launches. pdl launches the kernel early
-// behind the stream's previous kernel; wait_first makes it wait for that kernel before it
-// reads any input (otherwise it waits only before it completes).
+// behind the stream's previous kernel; wait_first 1 makes it wait for that kernel before it
+// reads any input, 0 only before it completes, 2 before anything but the page table and the
+// first pages that are not a sequence's last (the caller vouches those are older).
 ckl_status launch_partial(const ckl_decode_params* p, int G, bool direct, __half* out,
                           float* lse, float* part_o, float* part_lse, cudaStream_t stream,
                           int out_heads = 0, int head_offset = 0, bool pdl = false,
-                          const int2* seq_tab = nullptr, bool wait_first = false);
+                          const int2* seq_tab = nullptr, int wait_first = 0);
 // merge_states_kernel launched with PDL (seq_tab NULL: every row merges `stride` slots)
 ckl_status launch_merge(const float* part_o, const float* part_lse, __half* out, float* lse,
                         int rows, int stride, int Hq, int out_heads, int head_offset,

@@ -60,7 +60,10 @@ struct Args {
     float scale_log2;
     // launched early behind the previous kernel of the stream (programmatic dependent launch):
     // 1 = wait for it before reading any input (the general case: it may have written q, the
-    // page table or the caches); 0 = the inputs are older, wait only before completing
+    // page table or the caches); 0 = the inputs are older, wait only before completing;
+    // 2 = the page table and every page but each sequence's last are older: the producer
+    // issues the ring's first pages (last pages excluded) before it waits, every other read
+    // and every write waits
     int wait_first;
 };
 
@@ -94,7 +97,9 @@ decode_partial_kernel(const __grid_constant__ CUtensorMap tmK,
         tma_prefetch_desc(&tmV);
     }
     __syncthreads();
-    if (a.wait_first) pdl_wait();    // the set-up above overlapped the previous kernel's tail
+    // the set-up above overlapped the previous kernel's tail; in mode 2 the producer waits
+    // later, after the first pages are in flight
+    if (a.wait_first == 1 || (a.wait_first == 2 && warp != CONSUMERS)) pdl_wait();
     const uint64_t deadline = globaltimer() + a.timeout_ns;
     pdl_trigger();                   // a merge launched after us may be scheduled now
 
@@ -115,11 +120,18 @@ decode_partial_kernel(const __grid_constant__ CUtensorMap tmK,
         // ---------------------------------------------------------------- producer warp
         const uint64_t pol = policy_evict_first();
         int ok = 1, issued = 0;
+        bool waited = a.wait_first != 2;
         for (int base = 0; base < npg && ok; base += 32) {
             const int cnt = min(32, npg - base);
             const int my_page = lane < cnt ? __ldg(a.indices + page_beg + p0 + base + lane) : 0;
             for (int j = 0; j < cnt; j++) {
                 const int page = __shfl_sync(0xffffffffu, my_page, j);
+                // mode 2: a sequence's last page (the previous kernel may append to it) and
+                // anything past the ring's first fill come after the wait
+                if (!waited && (base + j >= STAGES || p0 + base + j == npages - 1)) {
+                    pdl_wait();
+                    waited = true;
+                }
                 if (lane == 0) {
                     const int i = base + j, s = i % STAGES;
                     if (i >= STAGES) ok = mbar_wait(&empty[s], ((i / STAGES) - 1) & 1, deadline, a.err);
@@ -133,6 +145,7 @@ decode_partial_kernel(const __grid_constant__ CUtensorMap tmK,
                 if (!ok) break;
             }
         }
+        if (!waited) pdl_wait();     // before the outputs this warp helps write
         // Every issued copy must land before the CTA reuses the ring or exits.
         if (lane == 0) {
             for (int s = 0; s < STAGES && s < issued; s++) {
@@ -406,7 +419,7 @@ ckl_status validate(const ckl_decode_params* p, int* G) {
 ckl_status launch_partial(const ckl_decode_params* p, int G, bool direct, __half* out,
                           float* lse, float* part_o, float* part_lse, cudaStream_t stream,
                           int out_heads, int head_offset, bool pdl, const int2* seq_tab,
-                          bool wait_first) {
+                          int wait_first) {
     const DeviceInfo* di = device_info();
     if (!di) return CKL_CUDA_ERROR;
     const KernelSetup* ks = setup(di);
@@ -439,7 +452,7 @@ ckl_status launch_partial(const ckl_decode_params* p, int G, bool direct, __half
     a.head_offset = head_offset;
     a.seq_tab = seq_tab;
     a.scale_log2 = p->sm_scale * LOG2E;
-    a.wait_first = wait_first ? 1 : 0;
+    a.wait_first = wait_first;
 
     void* args[] = {&tmK, &tmV, &a};
     dim3 grid((unsigned)(p->B * p->Hkv), (unsigned)p->num_chunks);
@@ -544,14 +557,14 @@ namespace attn {
 // decode_attention with the output rows of (b, h) at b*out_heads + head_offset + h.
 ckl_status decode_attention_rows(const ckl_decode_params* p, void* out, float* lse,
                                  void* workspace, size_t workspace_bytes, cudaStream_t s,
-                                 int out_heads, int head_offset) {
+                                 int out_heads, int head_offset, int wait_mode) {
     int G = 0;
     ckl_status st = validate(p, &G);
     if (st != CKL_OK || p->B == 0) return st;
     if (!out || !lse) return fail(CKL_INVALID_ARG, "out/lse are NULL");
     if (p->num_chunks == 1 && p->chunk_base == 0 && p->part_stride == 1)
         return launch_partial(p, G, true, static_cast<__half*>(out), lse, nullptr, nullptr, s,
-                              out_heads, head_offset, true, nullptr, true);
+                              out_heads, head_offset, true, nullptr, wait_mode);
     const size_t need = ckl_decode_workspace_size(p);
     if (!workspace || workspace_bytes < need)
         return fail(CKL_WORKSPACE_TOO_SMALL, "decode_attention needs %zu workspace bytes, got %zu",
@@ -560,7 +573,8 @@ ckl_status decode_attention_rows(const ckl_decode_params* p, void* out, float* l
     if ((uintptr_t)out & 7) return fail(CKL_INVALID_ARG, "out needs 8-byte alignment");
     float* part_o = static_cast<float*>(workspace);
     float* part_lse = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + part_o_bytes(p));
-    st = launch_partial(p, G, false, nullptr, nullptr, part_o, part_lse, s, 0, 0, true, nullptr, true);
+    st = launch_partial(p, G, false, nullptr, nullptr, part_o, part_lse, s, 0, 0, true, nullptr,
+                        wait_mode);
     if (st != CKL_OK) return st;
     return launch_merge(part_o, part_lse, static_cast<__half*>(out), lse, p->B * p->Hq, p->part_stride,
                         p->Hq, out_heads > 0 ? out_heads : p->Hq, head_offset, nullptr, 0, s);
@@ -574,7 +588,16 @@ extern "C" {
 ckl_status ckl_decode_attention(const ckl_decode_params* p, void* out, float* lse,
                                 void* workspace, size_t workspace_bytes, void* stream) {
     return decode_attention_rows(p, out, lse, workspace, workspace_bytes, (cudaStream_t)stream,
-                                 p ? p->Hq : 0, 0);
+                                 p ? p->Hq : 0, 0, 1);
+}
+
+ckl_status ckl_decode_attention_ex(const ckl_decode_params* p, void* out, float* lse,
+                                   void* workspace, size_t workspace_bytes, unsigned flags,
+                                   void* stream) {
+    if (flags & ~CKL_DECODE_CACHE_READY)
+        return fail(CKL_INVALID_ARG, "decode_attention_ex: unknown flags 0x%x", flags);
+    return decode_attention_rows(p, out, lse, workspace, workspace_bytes, (cudaStream_t)stream,
+                                 p ? p->Hq : 0, 0, (flags & CKL_DECODE_CACHE_READY) ? 2 : 1);
 }
 
 ckl_status ckl_decode_attention_gather(const ckl_decode_params* p, void* out_full,
@@ -585,7 +608,7 @@ ckl_status ckl_decode_attention_gather(const ckl_decode_params* p, void* out_ful
         return fail(CKL_INVALID_ARG, "decode_attention_gather: heads [%d, %d) outside [0, %d)",
                     head_offset, head_offset + p->Hq, Hq_total);
     return decode_attention_rows(p, out_full, lse_full, workspace, workspace_bytes,
-                                 (cudaStream_t)stream, Hq_total, head_offset);
+                                 (cudaStream_t)stream, Hq_total, head_offset, 1);
 }
 
 ckl_status ckl_validate_page_table(const int* h_indptr, const int* h_indices,

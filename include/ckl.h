@@ -124,6 +124,20 @@ CKL_API ckl_status ckl_merge_states(const float* part_o, const float* part_lse, 
 CKL_API ckl_status ckl_decode_attention(const ckl_decode_params* p, void* out, float* lse,
                                 void* workspace, size_t workspace_bytes, void* stream);
 
+/* ckl_decode_attention with flags (no reference counterpart: the reference launches its
+ * kernels in plain stream order). ckl_decode_attention may start behind the stream's
+ * previous kernel but reads nothing until that kernel has finished. With
+ * CKL_DECODE_CACHE_READY the caller vouches that the page table and every KV page except
+ * each sequence's last one were written before the previous kernel began (the usual decode
+ * step: the kernel before attention writes q and appends the new token to the last page);
+ * the call then reads the page table and starts streaming the first pages while that
+ * kernel finishes. q, the last pages and every write still wait for it. Same results as
+ * ckl_decode_attention. Unknown flag bits: CKL_INVALID_ARG. */
+#define CKL_DECODE_CACHE_READY 1u
+CKL_API ckl_status ckl_decode_attention_ex(const ckl_decode_params* p, void* out, float* lse,
+                                           void* workspace, size_t workspace_bytes,
+                                           unsigned flags, void* stream);
+
 /* Balanced split (no reference counterpart: the reference lists it as not done,
  * README.md:54). The pages of all (sequence, kv head) units are divided exactly evenly over
  * one wave of persistent CTAs (SMs x resident CTAs per SM), with a partial wherever a CTA's

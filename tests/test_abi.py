@@ -35,6 +35,12 @@ def test_library_exports_every_declared_symbol(ckl):
     assert names <= set(ckl._SIGS), names - set(ckl._SIGS)
 
 
+def test_decode_attention_ex_rejects_unknown_flags(ckl):
+    # checked on the host before anything else (no device needed)
+    st = ckl.lib().ckl_decode_attention_ex(None, None, None, None, 0, 0x2, None)
+    assert st == 1   # CKL_INVALID_ARG
+
+
 def test_version_and_error_string(ckl):
     assert "sm_100a" in ckl.version()
     assert isinstance(ckl.lib().ckl_last_error_string(), bytes)

@@ -91,6 +91,57 @@ def test_deterministic_repeat(ckl, oracle, dev):
     assert bool((a[0] == b[0]).all()) and bool((a[1] == b[1]).all())
 
 
+@pytest.mark.parametrize("force", [0, 5])
+def test_cache_ready_chain_equals_plain(ckl, oracle, dev, force):
+    """ckl_decode_attention_ex with CKL_DECODE_CACHE_READY in a chain where each call's q is
+    the previous call's output (written by the kernel it starts behind): every output equals
+    the plain entry point's bit for bit, launched back to back on one stream and replayed
+    from a CUDA graph; the first layer is checked against the fp64 oracle. The caches and
+    page tables are written before the chain starts, as the flag requires."""
+    import torch
+    lens = [5, 300, 2049, 4096]
+    layers = [to_dev(oracle.batch(lens, 32, 8, 40 + l), dev) for l in range(4)]
+    q0 = layers[0]["q"]
+
+    def run(ready, outs):
+        x = q0
+        for l, d in enumerate(layers):
+            dd = dict(d, q=x)
+            ckl.decode_attention(**dd, max_len=max(lens), force_chunks=force, out=outs[l][0],
+                                 lse=outs[l][1], workspace=ws, cache_ready=ready)
+            x = outs[l][0]
+
+    ws = torch.empty(64 << 20, dtype=torch.uint8, device=dev)
+    mk = lambda: [(torch.empty_like(q0), torch.empty((len(lens), 32), dtype=torch.float32,
+                                                     device=dev)) for _ in layers]
+    plain, ready, graphed = mk(), mk(), mk()
+    run(False, plain)
+    run(True, ready)
+    torch.cuda.synchronize()
+    ckl.check_device_error()
+    s = torch.cuda.Stream(device=dev)
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        run(True, graphed)                              # warm-up outside the capture
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        run(True, graphed)
+    for o, l in graphed:
+        o.zero_()
+        l.zero_()
+    g.replay()
+    torch.cuda.synchronize()
+    ckl.check_device_error()
+    for l in range(len(layers)):
+        for got in (ready[l], graphed[l]):
+            assert torch.equal(got[0], plain[l][0]) and torch.equal(got[1], plain[l][1]), l
+    bt = oracle.batch(lens, 32, 8, 40)
+    ref_o, ref_l = oracle.attention_ref(bt)
+    check(plain[0][0], plain[0][1], ref_o, ref_l, "cache-ready chain, layer 0")
+
+
 def test_partial_and_merge_entry_points(ckl, oracle, dev):
     """decode_partial + merge_states driven separately (the cascade suffix pattern:
     kv_start > 0, chunk_base > 0) against the oracle over the suffix keys."""
