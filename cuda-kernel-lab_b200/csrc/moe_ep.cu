@@ -214,7 +214,28 @@ __global__ void __launch_bounds__(256)
 ep_combine_kernel(const EpArgs p, const int* __restrict__ ids, const int* __restrict__ inv_perm,
                   const int* __restrict__ offsets, const float* __restrict__ wts,
                   __half* __restrict__ out, int T) {
+    // Each assignment's owner, slab row and weight come from the routing, which completed
+    // before the kernel we wait for was launched: look them up (from L2) before the wait, so
+    // that after the flags only the rows are left to read.
+    constexpr int KMAX = 8;                           // k <= 8 (the routing's bound)
+    const int t = blockIdx.x;
+    int own_j[KMAX], pos_j[KMAX];
+    float w_j[KMAX];
+#pragma unroll
+    for (int j = 0; j < KMAX; j++) {
+        own_j[j] = 0;
+        pos_j[j] = 0;
+        w_j[j] = 0.f;
+        if (t < T && j < p.k) {
+            const int i = t * p.k + j;
+            const int o = __ldcg(ids + i) / p.E_loc;
+            own_j[j] = o;
+            pos_j[j] = __ldcg(inv_perm + i) - __ldcg(offsets + o * p.E_loc);
+            w_j[j] = __ldcg(wts + i);
+        }
+    }
     pdl_wait();                                       // the down GEMM has completed
+    pdl_trigger();                                    // the next layer's routing may launch
     const unsigned epoch = next_epoch(p);
     uint8_t* own = p.win[p.rank];
     if ((int)threadIdx.x < p.world) {
@@ -223,16 +244,14 @@ ep_combine_kernel(const EpArgs p, const int* __restrict__ ids, const int* __rest
                    globaltimer() + p.timeout_ns, p.err);
     }
     __syncthreads();
-    const int t = blockIdx.x;
     if (t < T) {
         for (int c = threadIdx.x; c < p.d / 8; c += blockDim.x) {
             float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-            for (int j = 0; j < p.k; j++) {
-                const int i = t * p.k + j;
-                const int e = __ldg(ids + i);
-                const int o = e / p.E_loc;
-                const int pos = __ldg(inv_perm + i) - __ldg(offsets + o * p.E_loc);
-                const float w = __ldg(wts + i);
+#pragma unroll
+            for (int j = 0; j < KMAX; j++) {
+                if (j >= p.k) break;
+                const int o = own_j[j], pos = pos_j[j];
+                const float w = w_j[j];
                 const float4* src = reinterpret_cast<const float4*>(
                     p.win[o] + p.off_y + ((size_t)p.rank * p.cap + pos) * p.d * 4) + 2 * c;
                 const float4 v0 = __ldcg(src), v1 = __ldcg(src + 1);
