@@ -171,6 +171,7 @@ _SIGS = {
                                               C.c_void_p]),
     "ckl_gather_signal": (C.c_int, [C.POINTER(PeerGroup), C.c_int, C.c_void_p]),
     "ckl_gather_wait": (C.c_int, [C.POINTER(PeerGroup), C.c_void_p]),
+    "ckl_peer_barrier": (C.c_int, [C.POINTER(PeerGroup), C.c_void_p]),
     "ckl_moe_ep_window_bytes": (C.c_size_t, [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int]),
     "ckl_ep_window_alloc": (C.c_int, [C.c_size_t, C.POINTER(C.c_void_p), C.c_void_p]),
     "ckl_ep_window_open": (C.c_int, [C.c_void_p, C.POINTER(C.c_void_p)]),
@@ -872,6 +873,9 @@ class GatherGroup(IpcWindows):
 
     def wait(self, stream=None):
         check(lib().ckl_gather_wait(C.byref(self.group), _stream(stream)), "ckl_gather_wait")
+
+    def barrier(self, stream=None):
+        check(lib().ckl_peer_barrier(C.byref(self.group), _stream(stream)), "ckl_peer_barrier")
 
 
 def decode_attention_gather(p: DecodeParams, out_full_ptr, lse_full_ptr, Hq_total, head_offset,

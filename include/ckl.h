@@ -458,6 +458,14 @@ typedef struct ckl_peer_group {
 CKL_API ckl_status ckl_gather_signal(const ckl_peer_group* g, int root, void* stream);
 CKL_API ckl_status ckl_gather_wait(const ckl_peer_group* g, void* stream);
 
+/* Barrier of the group on the GPUs (no reference counterpart: the reference runs on one
+ * GPU): no rank's later kernels on `stream` run before every rank has reached its barrier
+ * call in stream order. For a double-buffered gather, where the root must have read a
+ * buffer back before any rank writes it again. Epoch flags in the same windows, bounded
+ * wait (CKL_TIMEOUT via ckl_check_device_error); every rank calls it the same number of
+ * times. */
+CKL_API ckl_status ckl_peer_barrier(const ckl_peer_group* g, void* stream);
+
 /* ======================================================================================
  * Expert-parallel MoE layer over NVLink peer memory (north star: "expert-parallel with a
  * token all-to-all for dispatch and combine"; the reference is single-GPU and has no

@@ -80,3 +80,31 @@ def test_gather_wait_gives_up_on_a_flag_nothing_sets(ckl, dev):
         torch.cuda.synchronize()
         L.free(w0)
         L.free(w1)
+
+
+def test_peer_barrier_gives_up_on_a_rank_that_never_arrives(ckl, dev):
+    """ckl_peer_barrier with a second window that no other rank writes: the barrier's bounded
+    wait gives up (CKL_TIMEOUT) and the context stays usable; a one-rank group passes its
+    barriers at once, many times in a row (epochs)."""
+    import torch
+    L = ckl._LibWindows
+    w0, _ = L.alloc(ckl.PEER_WINDOW_BYTES)
+    w1, _ = L.alloc(ckl.PEER_WINDOW_BYTES)
+    try:
+        g = ckl.PeerGroup(0, 2, (ckl.C.c_void_p * ckl.EP_MAX_RANKS)(w0, w1))
+        ckl.set_spin_timeout_ns(20_000_000)
+        ckl.check(ckl.lib().ckl_peer_barrier(ckl.C.byref(g), None), "barrier")  # rank 1 absent
+        torch.cuda.synchronize()
+        with pytest.raises(ckl.CklError) as e:
+            ckl.check_device_error()
+        assert e.value.status == 5
+        g1 = ckl.PeerGroup(0, 1, (ckl.C.c_void_p * ckl.EP_MAX_RANKS)(w1))
+        for _ in range(5):
+            ckl.check(ckl.lib().ckl_peer_barrier(ckl.C.byref(g1), None), "barrier")
+        torch.cuda.synchronize()
+        ckl.check_device_error()
+    finally:
+        ckl.set_spin_timeout_ns(1_000_000_000)
+        torch.cuda.synchronize()
+        L.free(w0)
+        L.free(w1)
