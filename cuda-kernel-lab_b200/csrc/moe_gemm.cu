@@ -433,7 +433,6 @@ __device__ __forceinline__ void gemm_body(const GemmArgs& a, uint8_t* ring, floa
     }
 }
 
-
 // grid = (quads, min(E, A) expert slots, ksplit); 9 warps (8 consumers + 1 producer).
 template <int BITS, bool SWIGLU, bool GROUPED, int OCC, int TM>
 __global__ void __launch_bounds__(GTHREADS, OCC)
