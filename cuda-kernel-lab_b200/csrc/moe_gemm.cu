@@ -444,14 +444,9 @@ moe_gemm_kernel(const GemmArgs a) {
     uint64_t* full = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(red) + C::RED);
     uint64_t* empty = full + MAX_STAGES;
 
-    if (a.dep == 1) pdl_wait();                          // offsets come from the previous kernel
-    int row_beg, n_e;
-    const int e = nth_active_expert(a.offsets, a.E, blockIdx.y, row_beg, n_e);
-    if (e < 0) {                                         // surplus slot of the upper bound
-        pdl_trigger();
-        return;
-    }
-    if (threadIdx.x == 0) {                              // enough for either ring layout
+    // the ring's barriers (enough for either layout) are set up while the previous kernel may
+    // still run; only the expert lookup waits for it (dep 1: the offsets are its output)
+    if (threadIdx.x == 0) {
         for (int s = 0; s < C::template Ring<1>::N; s++) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], CONSUMERS);
@@ -459,6 +454,13 @@ moe_gemm_kernel(const GemmArgs a) {
         fence_barrier_init();
     }
     __syncthreads();
+    if (a.dep == 1) pdl_wait();
+    int row_beg, n_e;
+    const int e = nth_active_expert(a.offsets, a.E, blockIdx.y, row_beg, n_e);
+    if (e < 0) {                                         // surplus slot of the upper bound
+        pdl_trigger();
+        return;
+    }
     // stages sized for the CTA's largest pass: one 8-row token tile, or TM
     if (TM == 1 || n_e <= 8)
         gemm_body<BITS, SWIGLU, GROUPED, OCC, TM, 1>(a, ring, red, full, empty, e, row_beg, n_e);
